@@ -1,0 +1,369 @@
+#!/usr/bin/env python
+"""GRU FP32 train-step benchmark (BASELINE metric: samples*timesteps/s).
+
+One step = forward + MSE loss + backward + (all-reduce for N > 1) + SGD
+lr 1e-2 of a 1-layer GRU, I = H = 256, T = 512, batch 64 per GPU (BASELINE
+config 2 at N = 1; weak scaling at N > 1, i.e. config 5's DP step with
+64 rows per rank).  ``--global-batch`` switches to config 5's strong-scaling
+form (global batch split evenly over the ranks).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+    python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N
+
+Rank 0 prints one JSON line.  Timing: W untimed warm-up steps, then exactly K
+steps, each bracketed by CUDA events on the launching stream, with a 256 MiB
+L2 flush between steps outside the events; barrier + synchronize on both
+sides; the per-step time is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "GRU fp32 train samples·timesteps/s at H=256, 1/2/4/8 B200 vs cuDNN & host CPU"
+UNIT = "samples*timesteps/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--batch-per-gpu", type=int, default=64)
+    ap.add_argument("--global-batch", type=int, default=0, help="strong scaling: split this batch over ranks")
+    ap.add_argument("--seq-len", type=int, default=512)
+    ap.add_argument("--input-size", type=int, default=256)
+    ap.add_argument("--hidden-size", type=int, default=256)
+    ap.add_argument("--layers", type=int, default=1)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-cudnn", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ---------------------------------------------------------------------------
+# clocks: nvidia-smi sampled during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.tmp = None
+
+    def __enter__(self):
+        try:
+            self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.tmp, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or self.tmp is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        with open(self.tmp.name) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[4:]))
+                except ValueError:
+                    continue
+        os.unlink(self.tmp.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        load = [r for r in rows if r[2] > 200.0] or rows
+        sm = sorted(r[0] for r in load)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in load:
+            for name, v in zip(names, r[3][1:]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": sorted(reasons), "samples": len(load),
+                "power_w_max": max(r[2] for r in rows)}
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the reference's own CPU implementation of the path
+# ---------------------------------------------------------------------------
+def run_reference(args, world, rank):
+    if rank != 0:
+        return 0
+    from oracle.cpu_baseline import time_cpu_train_step
+
+    B = args.global_batch // world if args.global_batch else args.batch_per_gpu
+    T, I, H = args.seq_len, args.input_size, args.hidden_size
+    # One step of the full workload takes about a second on a many-core host;
+    # cap the count so the whole run stays within a few minutes.
+    steps = max(1, min(args.steps, 10))
+    warm = max(1, min(args.warmup, 2))
+    r = time_cpu_train_step(B, T, I, H, warmup=warm, steps=steps)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": r["value"], "unit": UNIT, "n_gpus": world,
+        "steps": steps, "warmup": warm, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic N(0,1) x and target",
+        "config": {"workload": f"gru_train_step I={I} H={H} B={B} T={T} (rank-0 shard)", "global_batch": B,
+                   "seq_len": T, "input_size": I, "hidden_size": H, "layers": 1, "parallelism": "cpu"},
+        "cpu_baseline": {"value": r["value"], "unit": UNIT, "cores": r["cores"], "kind": "reference",
+                         "sample": f"torch.nn.GRU FP32 train step on host CPU ({r['cpu_model']}), "
+                                   f"full B={B},T={T} shard, {warm} warm-up + {steps} timed steps"},
+        "e2e": {"value": r["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# roofline bookkeeping
+# ---------------------------------------------------------------------------
+def fp32_peak_tflops(sm_mhz: float, sms: int = 148) -> float:
+    # 128 FP32 FMA lanes per SM, 2 FLOP per FMA.
+    return sms * 128 * 2 * sm_mhz * 1e6 / 1e12
+
+
+def recurrent_flops(b, T, H, bwd: bool) -> float:
+    # per timestep: the b x 3H x H recurrent product + the gate arithmetic
+    # (10 FLOP per element forward, 16 backward; transcendental = 1).
+    return T * (2.0 * b * 3 * H * H + (16 if bwd else 10) * b * H)
+
+
+def step_roofline_ms(b, T, H, sm_mhz: float, sms: int = 148) -> float:
+    p_fp32 = fp32_peak_tflops(sm_mhz, sms) * 1e12
+    bw_smem = sms * 128 * sm_mhz * 1e6  # bytes/s
+    w_bytes = 3 * H * H * 4
+    t_f = w_bytes / bw_smem + (2 * b * 3 * H * H + 10 * b * H) / p_fp32
+    t_b = w_bytes / bw_smem + (2 * b * 3 * H * H + 16 * b * H) / p_fp32
+    return 1e3 * T * (t_f + t_b)
+
+
+def load_traffic():
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except ValueError:
+            return {}
+    return {}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def timed_steps(step_fn, K, flush, torch):
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    for k in range(K):
+        flush()
+        evs[k][0].record()
+        step_fn(k)
+        evs[k][1].record()
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in evs]
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_env()
+    if args.impl == "reference":
+        return run_reference(args, world, rank)
+
+    import torch
+    import torch.distributed as dist
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    from rnn_kernel_b200 import GRU, DataParallelTrainer, _lib
+
+    B = args.global_batch // world if args.global_batch else args.batch_per_gpu
+    T, I, H, L = args.seq_len, args.input_size, args.hidden_size, args.layers
+    K, W = args.steps, max(3, args.warmup)
+    scaling = "strong" if args.global_batch else "weak"
+
+    torch.manual_seed(0)
+    model = GRU(I, H, num_layers=L).to(dev)
+    trainer = DataParallelTrainer(model, lr=1e-2)
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    x = torch.randn(B, T, I, device=dev, generator=g)
+    y = torch.randn(B, T, H, device=dev, generator=g)
+    flush_buf = torch.empty(256 * 1024 * 1024 // 4, device=dev)
+
+    def flush():
+        flush_buf.zero_()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(W):
+        trainer.step(x, y)
+    torch.cuda.synchronize()
+
+    # ---- timed region (device-resident inputs) ----
+    barrier()
+    torch.cuda.synchronize()
+    _lib.timing_enable(True)
+    _lib.timing_collect()
+    launches0 = _lib.launch_count()
+    with ClockSampler(local) as clk:
+        times = timed_steps(lambda k: trainer.step(x, y), K, flush, torch)
+    launches = _lib.launch_count() - launches0
+    _lib.timing_enable(False)
+    ktimes = _lib.timing_collect()
+    torch.cuda.synchronize()
+    barrier()
+    ms = sum(times) / K
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t)
+    clocks = clk.summary()
+    value = B * world * T / (ms / 1e3)
+
+    # ---- end to end through the public API from pinned host buffers ----
+    e2e = None
+    if not args.no_e2e:
+        xh = x.cpu().pin_memory()
+        yh = y.cpu().pin_memory()
+        lh = torch.empty(1, pin_memory=True)
+
+        def e2e_step(k):
+            xd = xh.to(dev, non_blocking=True)
+            yd = yh.to(dev, non_blocking=True)
+            loss = trainer.step(xd, yd)
+            lh.copy_(loss.reshape(1), non_blocking=True)
+
+        for _ in range(2):
+            e2e_step(0)
+        torch.cuda.synchronize()
+        barrier()
+        et = timed_steps(e2e_step, K, flush, torch)
+        ems = sum(et) / K
+        if world > 1:
+            t = torch.tensor([ems], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t)
+        e2e = {"value": B * world * T / (ems / 1e3), "unit": UNIT, "ms_per_step": ems,
+               "h2d_bytes_per_step": (x.numel() + y.numel()) * 4, "d2h_bytes_per_step": 4,
+               "note": "per rank: x and target copied from pinned host memory, loss copied back, every step"}
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return 0
+
+    # ---- kernel roofline (dominant kernel, measured live in the timed region) ----
+    sm_mhz = clocks.get("sm_mhz") or 1965.0
+    per_kind = {k: {"ms_per_launch": (tot / n if n else None), "launches": n, "ms_per_step": tot / K}
+                for k, (tot, n) in ktimes.items()}
+    dom = max(("fwd_recurrent", "bwd_recurrent"), key=lambda k: ktimes[k][0])
+    dom_ms = per_kind[dom]["ms_per_launch"]
+    flops = recurrent_flops(B, T, H, dom == "bwd_recurrent")
+    achieved = flops / (dom_ms / 1e3) / 1e12 if dom_ms else None
+    peak = fp32_peak_tflops(1965.0)
+    traffic = load_traffic().get(dom)
+    roofline = {
+        "bound": "fp32", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+        "frac": (achieved / peak) if achieved else None, "traffic": traffic,
+        "peak_source": "nominal FP32 CUDA-core peak 148 SM x 128 FMA/clk x 2 x 1965 MHz "
+                       "(MEASURED_PEAKS.json has HBM and bf16 tensor figures only)",
+        "flops_per_launch": flops,
+    }
+    t_roof = step_roofline_ms(B, T, H, 1965.0) * L
+    step_roof = {"t_roof_ms": t_roof, "frac": t_roof / ms,
+                 "definition": "T*(t_fwd+t_bwd), t = 3H^2*4B/SMEM_BW + (2*b*3H*H + {10|16}*b*H)/P_fp32, nominal peaks"}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
+        "dtype": "fp32", "data": "synthetic: x, target ~ N(0,1) per rank (seed 1000+rank); weights U(-1/16,1/16)",
+        "config": {"workload": f"gru_train_step 1-layer I={I} H={H} T={T}, batch {B}/GPU "
+                               f"(fwd + MSE + bwd + allreduce + SGD lr 1e-2)",
+                   "global_batch": B * world, "seq_len": T, "input_size": I, "hidden_size": H, "layers": L,
+                   "parallelism": f"dp{world}", "l2": "256 MiB flush between timed steps (outside the events)"},
+        "clocks": clocks,
+        "gpu_launches": int(launches),
+        "kernels": per_kind,
+        "roofline": roofline,
+        "step_roofline": step_roof,
+        "e2e": e2e,
+        "impl": "b200",
+    }
+
+    if world == 1 and not args.no_cudnn:
+        from torch import nn
+
+        torch.manual_seed(0)
+        ref = nn.GRU(I, H, num_layers=L, batch_first=True).to(dev)
+        ref.flatten_parameters()
+        opt = torch.optim.SGD(ref.parameters(), lr=1e-2)
+
+        def cudnn_step(k):
+            opt.zero_grad(set_to_none=True)
+            out, _ = ref(x)
+            torch.nn.functional.mse_loss(out, y).backward()
+            opt.step()
+
+        for _ in range(W):
+            cudnn_step(0)
+        torch.cuda.synchronize()
+        ct = timed_steps(cudnn_step, K, flush, torch)
+        cms = sum(ct) / K
+        line["cudnn"] = {"value": B * T / (cms / 1e3), "unit": UNIT, "ms_per_step": cms,
+                         "what": "torch.nn.GRU (cuDNN, TF32 off) same step on the same GPU",
+                         "speedup_of_b200": cms / ms}
+        del opt, ref
+
+    if world == 1 and not args.no_cpu_baseline:
+        from oracle.cpu_baseline import time_cpu_train_step
+
+        r = time_cpu_train_step(B, T, I, H, warmup=1, steps=2)
+        line["cpu_baseline"] = {"value": r["value"], "unit": UNIT, "cores": r["cores"], "kind": "reference",
+                                "sample": f"torch.nn.GRU FP32 train step on host CPU ({r['cpu_model']}), "
+                                          f"full B={B},T={T} workload, 1 warm-up + 2 timed steps"}
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

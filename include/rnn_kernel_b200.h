@@ -1,0 +1,97 @@
+/*
+ * rnn_kernel_b200 — C ABI of the B200 (sm_100a) FP32 GRU training path.
+ *
+ * Plain pointers and sizes only; every pointer is a device pointer unless
+ * stated otherwise, every tensor is dense row-major float32, and every call is
+ * stream-ordered on `stream` (a cudaStream_t, NULL = legacy default stream).
+ * No call synchronises the stream, allocates device memory or throws; each
+ * returns a status code (GRU_OK == 0) and on failure records a message that
+ * gru_last_error() returns (per calling thread).
+ *
+ * Shapes: B batch, T seq_len, I input_size, H hidden_size (1 <= H <= 256).
+ * Gate order is r, z, n and the weight layout is torch.nn.GRU's:
+ * w_ih [3H, I], w_hh [3H, H], b_ih [3H], b_hh [3H]; x is batch_first [B, T, I].
+ *
+ * Reference interface replaced (paths inside HanXuxx/RNN_kernel):
+ *   src/rnn_kernel/a100/prod/gru.py  — the Python ctypes / cuda-python
+ *   launchers `_launch_forward` (:226-301), `_launch_forward_no_cache`
+ *   (:304-376), `_launch_pack_hidden_prev` (:379-412),
+ *   `_launch_backward_sequence` (:415-487) plus the torch GEMMs around them in
+ *   `_A100GRUFunction.forward/backward` (:519-523, :569-578).
+ */
+#ifndef RNN_KERNEL_B200_H
+#define RNN_KERNEL_B200_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GRU_OK 0
+#define GRU_ERR_INVALID 1     /* bad shape / null pointer / workspace too small */
+#define GRU_ERR_CUDA 2        /* a CUDA runtime/driver call failed */
+#define GRU_ERR_UNSUPPORTED 3 /* device or shape outside the supported range */
+
+/* Message for the last failing call on this thread ("" if none). Replaces the
+ * RuntimeError text of `_check_cuda_error` (prod/gru.py:57-63). */
+const char* gru_last_error(void);
+
+/* 1 if `device` is a compute-capability 10.x (B200 class) GPU this library
+ * was built for, else 0.  Replaces `is_a100_available` (prod/gru.py:109-117). */
+int gru_device_supported(int device);
+
+/* Bytes of the forward stash for one layer: per (b, t) the gates r, z, n, the
+ * recurrent n pre-activation W_hn.h + b_hn and the step's input hidden state
+ * h_prev, i.e. B*T*5H floats.  Replaces the gate cache of `_launch_forward`
+ * (prod/gru.py:236-238) plus the packed h_prev (:379-412). */
+size_t gru_stash_bytes(int B, int T, int H);
+
+/* Device workspace `gru_forward` needs (input-gate buffer [B,T,3H]). */
+size_t gru_forward_workspace_bytes(int B, int T, int I, int H);
+
+/* One GRU layer forward.
+ *   out [B,T,H], hn [B,H] are written.
+ *   stash: gru_stash_bytes() bytes for a training forward, or NULL for the
+ *   inference (no-stash) path.
+ * Replaces `_A100GRUFunction.forward` (prod/gru.py:490-529) and
+ * `_a100_gru_forward_inference` (:583-617). */
+int gru_forward(const float* x, const float* h0, const float* w_ih, const float* w_hh,
+                const float* b_ih, const float* b_hh, float* out, float* hn, float* stash,
+                void* workspace, size_t workspace_bytes, int B, int T, int I, int H,
+                void* stream);
+
+/* Device workspace `gru_backward` needs. */
+size_t gru_backward_workspace_bytes(int B, int T, int I, int H);
+
+/* One GRU layer backward from the stash of a training `gru_forward`.
+ *   dout [B,T,H] or NULL (treated as zeros), dhn [B,H] or NULL (zeros).
+ *   Writes dh0 [B,H], dw_ih [3H,I], dw_hh [3H,H], db_ih [3H], db_hh [3H]
+ *   (overwritten, not accumulated) and dx [B,T,I] unless dx is NULL.
+ * Replaces `_A100GRUFunction.backward` (prod/gru.py:532-580). */
+int gru_backward(const float* dout, const float* dhn, const float* x, const float* w_ih,
+                 const float* w_hh, const float* stash, float* dx, float* dh0, float* dw_ih,
+                 float* dw_hh, float* db_ih, float* db_hh, void* workspace,
+                 size_t workspace_bytes, int B, int T, int I, int H, void* stream);
+
+/* ---- Telemetry (no reference counterpart: the reference had no kernel
+ * timers; its profiling scripts used torch.profiler / nsys, see
+ * scripts/profile_a100_h256_step.py).  Kernel kinds: 0 input-projection GEMM,
+ * 1 forward time loop, 2 backward time loop, 3 gradient GEMMs (+ split-K
+ * reduce), 4 bias-gradient column sums. ---- */
+
+/* Number of kernels this library has launched in this process. */
+unsigned long long gru_launch_count(void);
+
+/* Turn per-launch CUDA-event timing on (1) or off (0). */
+int gru_timing_enable(int on);
+
+/* Wait for the recorded events and return, per kernel kind, the summed device
+ * time in ms and the number of timed launches; clears the record. */
+int gru_timing_collect(double* total_ms, int* count, int n_kinds);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RNN_KERNEL_B200_H */

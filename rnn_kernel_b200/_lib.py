@@ -1,0 +1,88 @@
+"""ctypes binding of ``librnn_kernel_b200.so`` (the C ABI in ``include/rnn_kernel_b200.h``).
+
+The library is built in-tree by :mod:`rnn_kernel_b200.build`.  Loading it does
+not need a GPU; calling any compute entry point does.  There is no fallback:
+if the library is missing the call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+from . import build as _build
+
+_lock = threading.Lock()
+_lib = None
+
+_c_float_p = ctypes.c_void_p
+_size_t = ctypes.c_size_t
+_int = ctypes.c_int
+
+# name -> (restype, argtypes); mirrors include/rnn_kernel_b200.h
+SIGNATURES = {
+    "gru_last_error": (ctypes.c_char_p, []),
+    "gru_device_supported": (_int, [_int]),
+    "gru_stash_bytes": (_size_t, [_int, _int, _int]),
+    "gru_forward_workspace_bytes": (_size_t, [_int, _int, _int, _int]),
+    "gru_backward_workspace_bytes": (_size_t, [_int, _int, _int, _int]),
+    "gru_forward": (_int, [_c_float_p] * 9 + [ctypes.c_void_p, _size_t] + [_int] * 4 + [ctypes.c_void_p]),
+    "gru_backward": (_int, [_c_float_p] * 12 + [ctypes.c_void_p, _size_t] + [_int] * 4 + [ctypes.c_void_p]),
+    "gru_launch_count": (ctypes.c_ulonglong, []),
+    "gru_timing_enable": (_int, [_int]),
+    "gru_timing_collect": (_int, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int), _int]),
+}
+
+KERNEL_KINDS = ("input_gemm", "fwd_recurrent", "bwd_recurrent", "grad_gemm", "colsum")
+
+
+def timing_enable(on: bool) -> None:
+    load().gru_timing_enable(1 if on else 0)
+
+
+def timing_collect() -> dict:
+    """Per kernel kind: (total device ms, timed launches) since the last collect."""
+    n = len(KERNEL_KINDS)
+    tot = (ctypes.c_double * n)()
+    cnt = (ctypes.c_int * n)()
+    check(load().gru_timing_collect(tot, cnt, n), "gru_timing_collect")
+    return {k: (tot[i], cnt[i]) for i, k in enumerate(KERNEL_KINDS)}
+
+
+def launch_count() -> int:
+    return int(load().gru_launch_count())
+
+
+def library_path() -> Path:
+    return _build.LIB_PATH
+
+
+def load(build_if_missing: bool = True) -> ctypes.CDLL:
+    """Load (building first if needed and possible) the CUDA library."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = library_path()
+        if build_if_missing and _build.needs_build():
+            _build.build()
+        if not path.exists():
+            raise RuntimeError(f"rnn_kernel_b200 CUDA library not found at {path}; run "
+                               "`python -m rnn_kernel_b200.build`")
+        lib = ctypes.CDLL(str(path))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    msg = load().gru_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        raise RuntimeError(f"{what} failed (status {status}): {last_error()}")

@@ -1,0 +1,240 @@
+// C ABI of the B200 GRU training path (declarations and contract in
+// include/rnn_kernel_b200.h).
+
+#include <cuda_runtime.h>
+
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+
+#include "common.cuh"
+#include "../../include/rnn_kernel_b200.h"
+
+namespace gru {
+
+namespace {
+thread_local std::string g_last_error;
+std::mutex g_mu;
+std::map<std::tuple<int, int, int, int>, RecGeom> g_geom;  // (device, kind, B, H)
+std::map<int, int> g_sms;
+
+constexpr size_t kAlign = 256;
+
+int geometry(int kind, int B, int T, int H, int device, RecGeom* out) {
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_geom.find(std::make_tuple(device, kind, B, H));
+    if (it != g_geom.end()) {
+      *out = it->second;
+      out->T = T;
+      return GRU_OK;
+    }
+  }
+  RecGeom g{};
+  const int rc = kind == 0 ? rec_forward_geometry(B, T, H, device, &g)
+                           : rec_backward_geometry(B, T, H, device, &g);
+  if (rc != GRU_OK) return rc;
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_geom[std::make_tuple(device, kind, B, H)] = g;
+  *out = g;
+  return GRU_OK;
+}
+
+int check_shape(int B, int T, int I, int H) {
+  if (B < 0 || T < 0 || I < 1 || H < 1) {
+    set_error("invalid shape: need B >= 0, T >= 0, I >= 1, H >= 1");
+    return GRU_ERR_INVALID;
+  }
+  if (H > 256) {
+    set_error("hidden_size > 256 is not supported");
+    return GRU_ERR_UNSUPPORTED;
+  }
+  return GRU_OK;
+}
+
+int current_device(int* dev) {
+  GRU_CUDA_TRY(cudaGetDevice(dev));
+  int major = 0;
+  GRU_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, *dev));
+  if (major != 10) {
+    set_error("rnn_kernel_b200 requires a compute capability 10.x (sm_100a) GPU");
+    return GRU_ERR_UNSUPPORTED;
+  }
+  return GRU_OK;
+}
+
+struct BwdLayout {
+  size_t dgi, dgh, gemm, col, total;
+};
+
+BwdLayout bwd_layout(int B, int T, int I, int H, int device) {
+  const long BT = (long)B * T;
+  BwdLayout l{};
+  size_t off = 0;
+  l.dgi = off;
+  off = align_up(off + sizeof(float) * BT * 3 * H, kAlign);
+  l.dgh = off;
+  off = align_up(off + sizeof(float) * BT * 3 * H, kAlign);
+  l.gemm = off;
+  size_t g = gemm_ws_bytes(3 * H, H, (int)BT, device);
+  g = std::max(g, gemm_ws_bytes(3 * H, I, (int)BT, device));
+  g = std::max(g, gemm_ws_bytes((int)BT, I, 3 * H, device));
+  off = align_up(off + g, kAlign);
+  l.col = off;
+  off = align_up(off + colsum_ws_bytes(BT, 3 * H), kAlign);
+  l.total = off;
+  return l;
+}
+
+}  // namespace
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+void clear_error() { g_last_error.clear(); }
+
+int sm_count(int device) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_sms.find(device);
+  if (it != g_sms.end()) return it->second;
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) n = 148;
+  g_sms[device] = n;
+  return n;
+}
+
+}  // namespace gru
+
+using namespace gru;
+
+extern "C" {
+
+const char* gru_last_error(void) { return g_last_error.c_str(); }
+
+int gru_device_supported(int device) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+    cudaGetLastError();
+    return 0;
+  }
+  int major = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return major == 10 ? 1 : 0;
+}
+
+size_t gru_stash_bytes(int B, int T, int H) {
+  if (B <= 0 || T <= 0 || H <= 0) return 0;
+  return sizeof(float) * (size_t)B * T * 5 * H;
+}
+
+size_t gru_forward_workspace_bytes(int B, int T, int I, int H) {
+  if (B <= 0 || T <= 0 || H <= 0) return 0;
+  (void)I;
+  return align_up(sizeof(float) * (size_t)B * T * 3 * H, kAlign);
+}
+
+size_t gru_backward_workspace_bytes(int B, int T, int I, int H) {
+  if (B <= 0 || T <= 0 || H <= 0 || I <= 0) return 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    dev = 0;
+  }
+  return bwd_layout(B, T, I, H, dev).total;
+}
+
+int gru_forward(const float* x, const float* h0, const float* w_ih, const float* w_hh,
+                const float* b_ih, const float* b_hh, float* out, float* hn, float* stash,
+                void* workspace, size_t workspace_bytes, int B, int T, int I, int H,
+                void* stream_) {
+  clear_error();
+  int rc = check_shape(B, T, I, H);
+  if (rc) return rc;
+  if (B == 0) return GRU_OK;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (!h0 || !hn || (T > 0 && (!x || !w_ih || !w_hh || !b_ih || !b_hh || !out))) {
+    set_error("gru_forward: null tensor pointer");
+    return GRU_ERR_INVALID;
+  }
+  int dev = 0;
+  if ((rc = current_device(&dev))) return rc;
+  if (T == 0) {
+    GRU_CUDA_TRY(cudaMemcpyAsync(hn, h0, sizeof(float) * (size_t)B * H, cudaMemcpyDeviceToDevice, stream));
+    return GRU_OK;
+  }
+  if (!workspace || workspace_bytes < gru_forward_workspace_bytes(B, T, I, H)) {
+    set_error("gru_forward: workspace too small");
+    return GRU_ERR_INVALID;
+  }
+  float* G = static_cast<float*>(workspace);
+  GemmArgs ga{x, I, 1, w_ih, 1, I, G, 3 * H, b_ih, B * T, 3 * H, I};
+  if ((rc = gemm(ga, nullptr, 0, dev, stream, kKindInputGemm))) return rc;
+  RecGeom g{};
+  if ((rc = geometry(0, B, T, H, dev, &g))) return rc;
+  return launch_rec_forward(G, h0, w_hh, b_hh, out, hn, stash, g, stream);
+}
+
+int gru_backward(const float* dout, const float* dhn, const float* x, const float* w_ih,
+                 const float* w_hh, const float* stash, float* dx, float* dh0, float* dw_ih,
+                 float* dw_hh, float* db_ih, float* db_hh, void* workspace,
+                 size_t workspace_bytes, int B, int T, int I, int H, void* stream_) {
+  clear_error();
+  int rc = check_shape(B, T, I, H);
+  if (rc) return rc;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (!dw_ih || !dw_hh || !db_ih || !db_hh || (B > 0 && !dh0)) {
+    set_error("gru_backward: null gradient pointer");
+    return GRU_ERR_INVALID;
+  }
+  int dev = 0;
+  if ((rc = current_device(&dev))) return rc;
+  if (B == 0 || T == 0) {
+    GRU_CUDA_TRY(cudaMemsetAsync(dw_ih, 0, sizeof(float) * 3 * H * (size_t)I, stream));
+    GRU_CUDA_TRY(cudaMemsetAsync(dw_hh, 0, sizeof(float) * 3 * H * (size_t)H, stream));
+    GRU_CUDA_TRY(cudaMemsetAsync(db_ih, 0, sizeof(float) * 3 * H, stream));
+    GRU_CUDA_TRY(cudaMemsetAsync(db_hh, 0, sizeof(float) * 3 * H, stream));
+    if (B > 0) {
+      if (dhn) GRU_CUDA_TRY(cudaMemcpyAsync(dh0, dhn, sizeof(float) * (size_t)B * H, cudaMemcpyDeviceToDevice, stream));
+      else GRU_CUDA_TRY(cudaMemsetAsync(dh0, 0, sizeof(float) * (size_t)B * H, stream));
+    }
+    return GRU_OK;
+  }
+  if (!x || !w_ih || !w_hh || !stash) {
+    set_error("gru_backward: null input pointer");
+    return GRU_ERR_INVALID;
+  }
+  const BwdLayout l = bwd_layout(B, T, I, H, dev);
+  if (!workspace || workspace_bytes < l.total) {
+    set_error("gru_backward: workspace too small");
+    return GRU_ERR_INVALID;
+  }
+  char* ws = static_cast<char*>(workspace);
+  float* dGi = reinterpret_cast<float*>(ws + l.dgi);
+  float* dGh = reinterpret_cast<float*>(ws + l.dgh);
+  void* gws = ws + l.gemm;
+  const size_t gws_bytes = l.col - l.gemm;
+  RecGeom g{};
+  if ((rc = geometry(1, B, T, H, dev, &g))) return rc;
+  if ((rc = launch_rec_backward(dout, dhn, w_hh, stash, dGi, dGh, dh0, g, stream))) return rc;
+
+  const int BT = B * T;
+  const int H3 = 3 * H;
+  // dW_hh = dG_hh^T . h_prev   (h_prev is stash column block 4)
+  GemmArgs a1{dGh, 1, H3, stash + 4 * H, 5L * H, 1, dw_hh, H, nullptr, H3, H, BT};
+  if ((rc = gemm(a1, gws, gws_bytes, dev, stream, kKindGradGemm))) return rc;
+  // dW_ih = dG_ih^T . x
+  GemmArgs a2{dGi, 1, H3, x, I, 1, dw_ih, I, nullptr, H3, I, BT};
+  if ((rc = gemm(a2, gws, gws_bytes, dev, stream, kKindGradGemm))) return rc;
+  if (dx) {
+    // dx = dG_ih . W_ih
+    GemmArgs a3{dGi, H3, 1, w_ih, I, 1, dx, I, nullptr, BT, I, H3};
+    if ((rc = gemm(a3, gws, gws_bytes, dev, stream, kKindGradGemm))) return rc;
+  }
+  if ((rc = colsum(dGi, BT, H3, db_ih, ws + l.col, stream))) return rc;
+  if ((rc = colsum(dGh, BT, H3, db_hh, ws + l.col, stream))) return rc;
+  return GRU_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,107 @@
+// Shared helpers for the rnn_kernel_b200 CUDA sources (sm_100a only).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stddef.h>
+
+#include <string>
+
+namespace gru {
+
+// Per-thread last-error text behind gru_last_error().
+void set_error(const std::string& msg);
+void clear_error();
+
+#define GRU_CUDA_TRY(expr)                                                          \
+  do {                                                                              \
+    cudaError_t err__ = (expr);                                                     \
+    if (err__ != cudaSuccess) {                                                     \
+      ::gru::set_error(std::string("CUDA error: ") + cudaGetErrorString(err__) +    \
+                       " at " #expr);                                               \
+      return GRU_ERR_CUDA;                                                          \
+    }                                                                               \
+  } while (0)
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+// ---------------------------------------------------------------------------
+// Recurrent-kernel geometry.  One GRU layer's time loop runs on independent
+// thread-block clusters; every cluster owns `bc` batch rows and keeps the whole
+// W_hh distributed over its C CTAs (CTA c owns hidden units [c*Hc, c*Hc+Hc),
+// i.e. the rows r/z/n of those units).
+// ---------------------------------------------------------------------------
+struct RecGeom {
+  int B, T, H;
+  int C;    // CTAs per cluster (ceil(H/32), 1..8)
+  int Hc;   // hidden units owned by one CTA (<= 32)
+  int nw;   // warps per CTA = ceil(H/32): warp w covers k in [32w, 32w+32)
+  int bc;   // batch rows per cluster
+  int bcp;  // bc rounded up to the GEMV sub-chunk
+  int pd;   // prefetch depth of the per-step input ring (steps in flight)
+  int nclusters;
+  size_t smem;  // dynamic shared memory bytes per CTA
+};
+
+constexpr int kSub = 4;  // batch rows per GEMV sub-chunk
+
+int rec_forward_geometry(int B, int T, int H, int device, RecGeom* g);
+int rec_backward_geometry(int B, int T, int H, int device, RecGeom* g);
+
+int launch_rec_forward(const float* G, const float* h0, const float* w_hh, const float* b_hh,
+                       float* out, float* hn, float* stash, const RecGeom& g,
+                       cudaStream_t stream);
+int launch_rec_backward(const float* dout, const float* dhn, const float* w_hh,
+                        const float* stash, float* dGi, float* dGh, float* dh0,
+                        const RecGeom& g, cudaStream_t stream);
+
+// ---------------------------------------------------------------------------
+// Dense FP32-accurate contraction  C[m, n] = sum_k A(m, k) * B(k, n) (+ bias[n])
+// with A(m, k) = A[m*sam + k*sak] and B(k, n) = B[k*sbk + n*sbn] (one of each
+// pair of strides is 1).  `ws` provides split-K partials; gemm_ws_bytes() says
+// how many bytes a given shape needs.
+// ---------------------------------------------------------------------------
+struct GemmArgs {
+  const float* A; long sam, sak;
+  const float* B; long sbk, sbn;
+  float* C; long ldc;
+  const float* bias;  // [N] or null
+  int M, N, K;
+};
+size_t gemm_ws_bytes(int M, int N, int K, int device);
+int gemm(const GemmArgs& a, void* ws, size_t ws_bytes, int device, cudaStream_t stream, int kind);
+
+// Column sums of a row-major [rows, cols] matrix into out[cols] (fp64
+// accumulation, deterministic two-pass).  ws needs colsum_ws_bytes().
+size_t colsum_ws_bytes(long rows, int cols);
+int colsum(const float* X, long rows, int cols, float* out, void* ws, cudaStream_t stream);
+
+int sm_count(int device);
+
+// ---------------------------------------------------------------------------
+// Launch accounting and optional per-kernel CUDA-event timing (host side).
+// Every kernel launch of this library goes through a LaunchScope so that
+// gru_launch_count() is exact and gru_timing_collect() can report per-kind
+// device time.
+// ---------------------------------------------------------------------------
+enum KernelKind {
+  kKindInputGemm = 0,   // x . W_ih^T + b_ih
+  kKindFwdRecurrent = 1,
+  kKindBwdRecurrent = 2,
+  kKindGradGemm = 3,    // dW_hh, dW_ih, dx contractions (+ split-K reduce)
+  kKindColsum = 4,      // db_ih / db_hh
+  kKindCount = 5
+};
+
+class LaunchScope {
+ public:
+  LaunchScope(int kind, cudaStream_t stream, int launches = 1);
+  ~LaunchScope();
+ private:
+  int kind_;
+  cudaStream_t stream_;
+  void* start_;
+};
+
+}  // namespace gru

@@ -1,0 +1,76 @@
+"""Data-parallel GRU training over one process per GPU (NCCL over NVLink).
+
+The reference has no distributed code; this is the B200 build's DP layer for
+BASELINE config 5 (global batch sharded evenly across 1/2/4/8 GPUs, MSE per
+shard, gradients all-reduced, SGD).
+
+Design: all parameters of the model are re-pointed into ONE flat FP32 buffer
+and their ``.grad`` into ONE flat gradient buffer.  Autograd accumulates each
+layer's gradients into that buffer in place, so a step is::
+
+    grad.zero_(); loss = mse(model(x), y); loss.backward()
+    all_reduce(grad, SUM)                      # one NCCL call, ~1.6 MB/layer
+    flat_params.add_(grad, alpha=-lr / world)  # SGD on the mean gradient
+
+i.e. one collective and one fused update kernel per step, independent of the
+number of layers.  The module is any ``nn.Module`` (the B200 :class:`GRU` on
+GPUs; ``torch.nn.GRU`` on CPU ``gloo`` ranks in the tests of this logic).
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+import torch.nn.functional as F
+
+
+def flatten_parameters_(module: nn.Module):
+    """Re-point every parameter of ``module`` into one flat buffer and give each
+    a ``.grad`` view into one flat gradient buffer.  Returns ``(flat, grad)``."""
+    params = [p for p in module.parameters() if p.requires_grad]
+    if not params:
+        raise ValueError("module has no trainable parameters")
+    dev, dt = params[0].device, params[0].dtype
+    flat = torch.empty(sum(p.numel() for p in params), device=dev, dtype=dt)
+    grad = torch.zeros_like(flat)
+    off = 0
+    with torch.no_grad():
+        for p in params:
+            n = p.numel()
+            flat[off:off + n].copy_(p.detach().reshape(-1))
+            p.data = flat[off:off + n].view_as(p)
+            p.grad = grad[off:off + n].view_as(p)
+            off += n
+    return flat, grad
+
+
+class DataParallelTrainer:
+    """SGD data-parallel trainer: shard-local fwd/bwd, one all-reduce, one update."""
+
+    def __init__(self, module: nn.Module, lr: float = 1e-2,
+                 process_group: Optional[dist.ProcessGroup] = None) -> None:
+        self.module = module
+        self.lr = float(lr)
+        self.group = process_group
+        self.world = dist.get_world_size(process_group) if dist.is_available() and dist.is_initialized() else 1
+        self.flat, self.grad = flatten_parameters_(module)
+        if self.world > 1:
+            # Every rank starts from rank 0's weights.
+            dist.broadcast(self.flat, src=0, group=process_group)
+
+    def loss(self, x: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
+        out, _ = self.module(x)
+        return F.mse_loss(out, target)
+
+    def step(self, x: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
+        """One train step on this rank's shard; returns the shard loss (detached)."""
+        self.grad.zero_()
+        loss = self.loss(x, target)
+        loss.backward()
+        if self.world > 1:
+            dist.all_reduce(self.grad, op=dist.ReduceOp.SUM, group=self.group)
+        with torch.no_grad():
+            self.flat.add_(self.grad, alpha=-self.lr / self.world)
+        return loss.detach()

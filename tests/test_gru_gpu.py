@@ -1,0 +1,147 @@
+"""GPU parity of the B200 GRU against torch.nn.GRU FP32 (and the fixtures)."""
+import numpy as np
+import pytest
+import torch
+
+from rnn_kernel_b200 import GRU, from_torch_gru
+from rnn_kernel_b200 import _lib
+from tests import golden_io
+from tests.gpu_parity import ATOL, RTOL, assert_parity, run_pair
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("case", golden_io.CASES)
+def test_golden_fixtures(case):
+    d = golden_io.load(case)
+    L, H, I = d["L"], d["H"], d["I"]
+    m = GRU(I, H, num_layers=L).cuda()
+    with torch.no_grad():
+        for l in range(L):
+            for p in ("weight_ih", "weight_hh", "bias_ih", "bias_hh"):
+                getattr(m, f"{p}_l{l}").copy_(torch.from_numpy(d[f"{p}_l{l}"]))
+    x = torch.from_numpy(d["x"]).cuda().requires_grad_(True)
+    h0 = torch.from_numpy(d["h0"]).cuda().requires_grad_(True)
+    out, hn = m(x, h0)
+    if d["mse"]:
+        torch.nn.functional.mse_loss(out, torch.from_numpy(d["target"]).cuda()).backward()
+    else:
+        torch.autograd.backward([out, hn], [torch.from_numpy(d["grad_out"]).cuda(),
+                                            torch.from_numpy(d["grad_h"]).cuda()])
+    got = {"out": out, "hn": hn, "dx": x.grad, "dh0": h0.grad}
+    for n, p in m.named_parameters():
+        got["d" + n] = p.grad
+    for k, v in got.items():
+        v = v.detach().double().cpu().numpy()
+        np.testing.assert_allclose(v, d[f"custom64_{k}"], rtol=RTOL, atol=ATOL, err_msg=f"{k} vs CustomGRU fp64")
+        np.testing.assert_allclose(v, d[f"torch32_{k}"], rtol=RTOL, atol=ATOL, err_msg=f"{k} vs nn.GRU fp32")
+
+
+@pytest.mark.parametrize("I,H,L,B,T", [
+    (1, 1, 1, 1, 1), (5, 7, 1, 3, 5), (4, 16, 2, 2, 8), (16, 33, 1, 3, 11), (1, 256, 1, 2, 5),
+    (16, 256, 4, 2, 5), (3, 31, 1, 5, 3), (9, 64, 3, 4, 9), (300, 40, 1, 2, 4),
+])
+def test_small_shapes(I, H, L, B, T):
+    mine, theirs = run_pair(I, H, L, B, T, seed=1000 + 10 * L + I + H)
+    assert_parity(mine, theirs)
+
+
+@pytest.mark.parametrize("H", [64, 96, 128, 129, 130, 160, 192, 256])
+def test_hidden_sweep_config3(H):
+    # input_size=H, batch=64, seq_len=256, seed = H.
+    mine, theirs = run_pair(H, H, 1, 64, 256, seed=H)
+    assert_parity(mine, theirs)
+
+
+def test_prod_shape_config2():
+    # I=H=256, B=64, T=512, h0=0, MSE against N(0,1) target.
+    mine, theirs = run_pair(256, 256, 1, 64, 512, seed=2, loss="mse", h0_scale=0)
+    assert_parity(mine, theirs)
+
+
+def test_prod_shape_random_grads():
+    # Same shape, unit-scale upstream gradients (much larger dW than the MSE case).
+    mine, theirs = run_pair(256, 256, 1, 64, 512, seed=3)
+    assert_parity(mine, theirs)
+
+
+def test_stacked_config4():
+    # 2 layers, I=128, H=256, B=128, T=1024, h0 ~ 0.1*N(0,1), loss sum(out^2).
+    mine, theirs = run_pair(128, 256, 2, 128, 1024, seed=4, loss="sumsq", h0_scale=0.1)
+    assert_parity(mine, theirs)
+
+
+@pytest.mark.parametrize("B,T", [(257, 6), (1100, 3), (3000, 2)])
+def test_large_batch_many_clusters(B, T):
+    mine, theirs = run_pair(8, 64, 1, B, T, seed=B)
+    assert_parity(mine, theirs)
+
+
+def test_hn_only_loss_grad_output_none():
+    mine, theirs = run_pair(6, 48, 2, 3, 7, seed=5, loss="hn_only")
+    assert_parity(mine, theirs)
+
+
+@pytest.mark.parametrize("L", [1, 2, 3])
+def test_inference_paths_match(L):
+    torch.manual_seed(2133 + L)
+    ref = torch.nn.GRU(16, 130, num_layers=L, batch_first=True)
+    x = torch.randn(3, 9, 16)
+    h0 = torch.randn(L, 3, 130)
+    with torch.no_grad():
+        r_out, r_hn = ref(x, h0)
+    m = from_torch_gru(ref.cuda())
+    with torch.no_grad():
+        o1, h1 = m(x.cuda(), h0.cuda())
+    o2, h2 = m.forward_inference(x.cuda(), h0.cuda())
+    assert not o1.requires_grad and not o2.requires_grad
+    for o, h in ((o1, h1), (o2, h2)):
+        torch.testing.assert_close(o.cpu(), r_out, rtol=RTOL, atol=ATOL)
+        torch.testing.assert_close(h.cpu(), r_hn, rtol=RTOL, atol=ATOL)
+
+
+def test_sequence_chunking_matches_full_bptt():
+    # Mirrors tests/test_sequence_chunking.py: carried hidden state across chunks.
+    torch.manual_seed(123)
+    m = GRU(3, 40, num_layers=2).cuda()
+    x = torch.randn(2, 11, 3, device="cuda")
+    y = torch.randn(2, 11, 40, device="cuda")
+    out, _ = m(x)
+    full = torch.nn.functional.mse_loss(out, y)
+    g_full = torch.autograd.grad(full, list(m.parameters()))
+    outs, h = [], None
+    for s in range(0, 11, 4):
+        o, h = m(x[:, s:s + 4], h)
+        outs.append(o)
+    chunk = torch.nn.functional.mse_loss(torch.cat(outs, 1), y)
+    g_chunk = torch.autograd.grad(chunk, list(m.parameters()))
+    torch.testing.assert_close(chunk, full, rtol=1e-6, atol=1e-6)
+    for a, b in zip(g_chunk, g_full):
+        torch.testing.assert_close(a, b, rtol=RTOL, atol=ATOL)
+
+
+def test_empty_batch_and_sequence():
+    m = GRU(4, 8).cuda()
+    h0 = torch.randn(1, 3, 8, device="cuda", requires_grad=True)
+    out, hn = m(torch.randn(3, 0, 4, device="cuda"), h0)
+    assert out.shape == (3, 0, 8)
+    torch.testing.assert_close(hn, h0)
+    hn.sum().backward()
+    torch.testing.assert_close(h0.grad, torch.ones_like(h0))
+    out, hn = m(torch.randn(0, 5, 4, device="cuda"))
+    assert out.shape == (0, 5, 8) and hn.shape == (1, 0, 8)
+
+
+def test_native_library_is_what_runs():
+    before = _lib.launch_count()
+    mine, theirs = run_pair(4, 32, 1, 2, 3, seed=7)
+    assert _lib.launch_count() > before
+    assert_parity(mine, theirs)
+
+
+def test_rejects_bad_inputs_on_gpu():
+    m = GRU(4, 8).cuda()
+    with pytest.raises(RuntimeError, match="float32"):
+        m(torch.randn(2, 3, 4, device="cuda", dtype=torch.float64))
+    with pytest.raises(ValueError):
+        m(torch.randn(2, 3, 5, device="cuda"))
