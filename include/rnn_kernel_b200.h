@@ -33,6 +33,9 @@ extern "C" {
 #define GRU_ERR_CUDA 2        /* a CUDA runtime/driver call failed */
 #define GRU_ERR_UNSUPPORTED 3 /* device or shape outside the supported range */
 
+/* Bits of the device status word (gru_device_status). */
+#define GRU_STATUS_WAIT_TIMEOUT 1 /* a kernel's bounded inter-CTA wait expired */
+
 /* Message for the last failing call on this thread ("" if none). Replaces the
  * RuntimeError text of `_check_cuda_error` (prod/gru.py:57-63). */
 const char* gru_last_error(void);
@@ -79,6 +82,14 @@ int gru_backward(const float* dout, const float* dhn, const float* x, const floa
  * scripts/profile_a100_h256_step.py).  Kernel kinds: 0 input-projection GEMM,
  * 1 forward time loop, 2 backward time loop, 3 gradient GEMMs (+ split-K
  * reduce), 4 bias-gradient column sums. ---- */
+
+/* Device status word of the current device: 0 when every kernel so far ran
+ * to completion, else GRU_STATUS_* bits (a bounded wait inside a time-loop
+ * kernel expired; results of that launch are invalid).  Synchronises the
+ * device.  reset != 0 clears the word.  Returns -1 (and sets the error text)
+ * if it cannot be read.  No reference counterpart: the reference's waits
+ * were grid.sync() calls with no bound. */
+int gru_device_status(int reset);
 
 /* Number of kernels this library has launched in this process. */
 unsigned long long gru_launch_count(void);

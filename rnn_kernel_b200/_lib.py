@@ -28,6 +28,7 @@ SIGNATURES = {
     "gru_backward_workspace_bytes": (_size_t, [_int, _int, _int, _int]),
     "gru_forward": (_int, [_c_float_p] * 9 + [ctypes.c_void_p, _size_t] + [_int] * 4 + [ctypes.c_void_p]),
     "gru_backward": (_int, [_c_float_p] * 12 + [ctypes.c_void_p, _size_t] + [_int] * 4 + [ctypes.c_void_p]),
+    "gru_device_status": (_int, [_int]),
     "gru_launch_count": (ctypes.c_ulonglong, []),
     "gru_timing_enable": (_int, [_int]),
     "gru_timing_collect": (_int, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int), _int]),
@@ -47,6 +48,14 @@ def timing_collect() -> dict:
     cnt = (ctypes.c_int * n)()
     check(load().gru_timing_collect(tot, cnt, n), "gru_timing_collect")
     return {k: (tot[i], cnt[i]) for i, k in enumerate(KERNEL_KINDS)}
+
+
+def device_status(reset: bool = False) -> int:
+    """The device status word (0 = every bounded wait completed); synchronises."""
+    st = load().gru_device_status(1 if reset else 0)
+    if st < 0:
+        raise RuntimeError(f"gru_device_status failed: {last_error()}")
+    return st
 
 
 def launch_count() -> int:

@@ -124,6 +124,13 @@ int gru_device_supported(int device) {
   return major == 10 ? 1 : 0;
 }
 
+int gru_device_status(int reset) {
+  clear_error();
+  int st = 0;
+  if (read_device_status(reset, &st) != GRU_OK) return -1;
+  return st;
+}
+
 size_t gru_stash_bytes(int B, int T, int H) {
   if (B <= 0 || T <= 0 || H <= 0) return 0;
   return sizeof(float) * (size_t)B * T * 5 * H;
@@ -223,10 +230,10 @@ int gru_backward(const float* dout, const float* dhn, const float* x, const floa
   const int H3 = 3 * H;
   // dW_hh = dG_hh^T . h_prev   (h_prev is stash column block 4)
   GemmArgs a1{dGh, 1, H3, stash + 4 * H, 5L * H, 1, dw_hh, H, nullptr, H3, H, BT};
-  if ((rc = gemm(a1, gws, gws_bytes, dev, stream, kKindGradGemm))) return rc;
+  if ((rc = gemm(a1, gws, gws_bytes, dev, stream, kKindGradGemm, true))) return rc;
   // dW_ih = dG_ih^T . x
   GemmArgs a2{dGi, 1, H3, x, I, 1, dw_ih, I, nullptr, H3, I, BT};
-  if ((rc = gemm(a2, gws, gws_bytes, dev, stream, kKindGradGemm))) return rc;
+  if ((rc = gemm(a2, gws, gws_bytes, dev, stream, kKindGradGemm, true))) return rc;
   if (dx) {
     // dx = dG_ih . W_ih
     GemmArgs a3{dGi, H3, 1, w_ih, I, 1, dx, I, nullptr, BT, I, H3};

@@ -38,14 +38,20 @@ struct RecGeom {
   int Hc;   // hidden units owned by one CTA (<= 32)
   int nw;   // warps per CTA = ceil(H/32): warp w covers k in [32w, 32w+32)
   int bc;   // batch rows per cluster
-  int bcp;  // bc rounded up to the GEMV sub-chunk
+  int R;    // batch rows per GEMV sub-chunk (<= kMaxRows)
+  int bcp;  // bc rounded up to a multiple of R
   int pd;   // prefetch depth of the per-step input ring (steps in flight)
   int nclusters;
+  int max_clusters;  // clusters of this kernel resident at once on the device
+  // Shared-memory layout, offsets in floats from the dynamic base; every
+  // region starts on a 16-byte boundary (float4 accesses).
+  int off1, off2, off3;
   size_t smem;  // dynamic shared memory bytes per CTA
 };
 
-constexpr int kSub = 4;  // batch rows per GEMV sub-chunk
+constexpr int kMaxRows = 8;  // largest GEMV sub-chunk (batch rows)
 
+int read_device_status(int reset, int* status);
 int rec_forward_geometry(int B, int T, int H, int device, RecGeom* g);
 int rec_backward_geometry(int B, int T, int H, int device, RecGeom* g);
 
@@ -70,7 +76,9 @@ struct GemmArgs {
   int M, N, K;
 };
 size_t gemm_ws_bytes(int M, int N, int K, int device);
-int gemm(const GemmArgs& a, void* ws, size_t ws_bytes, int device, cudaStream_t stream, int kind);
+// exact = true: FP64 products and accumulation (weight-gradient contractions).
+int gemm(const GemmArgs& a, void* ws, size_t ws_bytes, int device, cudaStream_t stream, int kind,
+         bool exact = false);
 
 // Column sums of a row-major [rows, cols] matrix into out[cols] (fp64
 // accumulation, deterministic two-pass).  ws needs colsum_ws_bytes().

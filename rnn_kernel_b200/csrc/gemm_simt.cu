@@ -13,8 +13,12 @@ namespace {
 constexpr int BM = 64, BN = 64, BK = 16;
 
 // C tile (or split-K partial) = A(m, k) B(k, n) over k in [k0, k1).
+// Acc = double: every FP32 x FP32 product is exact in FP64 and the sum is
+// accumulated in FP64 (used for the weight-gradient contractions whose K is
+// B*T); Acc = float: plain FP32 FMA (K = I or 3H).
+template <typename Acc>
 __global__ void __launch_bounds__(256)
-gemm_simt_kernel(GemmArgs a, int kchunk, float* partial) {
+gemm_simt_kernel(GemmArgs a, int kchunk, Acc* partial) {
   __shared__ float As[BK][BM + 4];
   __shared__ float Bs[BK][BN + 4];
   const int tid = threadIdx.x;
@@ -22,7 +26,7 @@ gemm_simt_kernel(GemmArgs a, int kchunk, float* partial) {
   const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
   const int k0 = blockIdx.z * kchunk;
   const int k1 = min(a.K, k0 + kchunk);
-  float acc[4][4] = {};
+  Acc acc[4][4] = {};
   const bool a_kfast = (a.sak == 1);
   const bool b_nfast = (a.sbn == 1);
   for (int kt = k0; kt < k1; kt += BK) {
@@ -43,7 +47,7 @@ gemm_simt_kernel(GemmArgs a, int kchunk, float* partial) {
     __syncthreads();
 #pragma unroll
     for (int kk = 0; kk < BK; ++kk) {
-      float av[4], bv[4];
+      Acc av[4], bv[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) av[i] = As[kk][ty * 4 + i];
 #pragma unroll
@@ -51,7 +55,7 @@ gemm_simt_kernel(GemmArgs a, int kchunk, float* partial) {
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        for (int j = 0; j < 4; ++j) acc[i][j] = fma(av[i], bv[j], acc[i][j]);
     }
     __syncthreads();
   }
@@ -66,13 +70,14 @@ gemm_simt_kernel(GemmArgs a, int kchunk, float* partial) {
       if (partial != nullptr) {
         partial[((size_t)blockIdx.z * a.M + m) * a.N + n] = acc[i][j];
       } else {
-        a.C[(long)m * a.ldc + n] = acc[i][j] + (a.bias ? a.bias[n] : 0.0f);
+        a.C[(long)m * a.ldc + n] = (float)(acc[i][j] + (a.bias ? (Acc)a.bias[n] : (Acc)0));
       }
     }
   }
 }
 
-__global__ void splitk_reduce_kernel(const float* partial, int S, GemmArgs a) {
+template <typename Acc>
+__global__ void splitk_reduce_kernel(const Acc* partial, int S, GemmArgs a) {
   const long MN = (long)a.M * a.N;
   for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < MN; e += (long)gridDim.x * blockDim.x) {
     double s = 0.0;
@@ -114,30 +119,37 @@ constexpr int kColChunks = 256;
 
 size_t gemm_ws_bytes(int M, int N, int K, int device) {
   const int S = splits_for(M, N, K, device);
-  return S > 1 ? sizeof(float) * (size_t)S * M * N : 0;
+  return S > 1 ? sizeof(double) * (size_t)S * M * N : 0;
 }
 
-int gemm(const GemmArgs& a, void* ws, size_t ws_bytes, int device, cudaStream_t stream, int kind) {
-  if (a.M <= 0 || a.N <= 0) return GRU_OK;
+template <typename Acc>
+int gemm_impl(const GemmArgs& a, void* ws, size_t ws_bytes, int device, cudaStream_t stream, int kind) {
   const int S = (a.K > 0 && ws != nullptr) ? splits_for(a.M, a.N, a.K, device) : 1;
   const int kchunk = a.K > 0 ? ceil_div(ceil_div(a.K, S), BK) * BK : BK;
   dim3 grid(ceil_div(a.N, BN), ceil_div(a.M, BM), S);
-  float* partial = nullptr;
+  Acc* partial = nullptr;
   if (S > 1) {
     if (ws_bytes < gemm_ws_bytes(a.M, a.N, a.K, device)) {
       set_error("gemm: workspace too small");
       return GRU_ERR_INVALID;
     }
-    partial = static_cast<float*>(ws);
+    partial = static_cast<Acc*>(ws);
   }
   LaunchScope scope(kind, stream, S > 1 ? 2 : 1);
-  gemm_simt_kernel<<<grid, 256, 0, stream>>>(a, kchunk, partial);
+  gemm_simt_kernel<Acc><<<grid, 256, 0, stream>>>(a, kchunk, partial);
   GRU_CUDA_TRY(cudaGetLastError());
   if (S > 1) {
-    splitk_reduce_kernel<<<sm_count(device) * 4, 256, 0, stream>>>(partial, S, a);
+    splitk_reduce_kernel<Acc><<<sm_count(device) * 4, 256, 0, stream>>>(partial, S, a);
     GRU_CUDA_TRY(cudaGetLastError());
   }
   return GRU_OK;
+}
+
+int gemm(const GemmArgs& a, void* ws, size_t ws_bytes, int device, cudaStream_t stream, int kind,
+         bool exact) {
+  if (a.M <= 0 || a.N <= 0) return GRU_OK;
+  return exact ? gemm_impl<double>(a, ws, ws_bytes, device, stream, kind)
+               : gemm_impl<float>(a, ws, ws_bytes, device, stream, kind);
 }
 
 size_t colsum_ws_bytes(long rows, int cols) { return sizeof(double) * (size_t)kColChunks * cols; }

@@ -12,20 +12,30 @@
 //   barrier and no co-residency requirement on the batch size.
 // * Forward, per step: every CTA multiplies its 3*Hc rows with the full
 //   h_{t-1} of its cluster's batch rows (held in its own shared memory), does
-//   the gate math for its units, and writes the new h slice into the next
-//   h buffer of every CTA of the cluster through distributed shared memory.
-//   One cluster barrier per step; the h buffer is double-buffered.
+//   the gate math for its units, and pushes the new h slice into the next
+//   h buffer of every CTA of the cluster with `st.async` remote stores that
+//   complete bytes on the receiver's mbarrier.  The receiver waits on its own
+//   mbarrier only: there is no per-step cluster barrier and no fence that
+//   would wait for the step's global stores.  h is double-buffered.
 // * Backward, per step: every CTA computes the pointwise backward for its
 //   units, then its share of dh_{t-1} = dG_hh . W_hh over all k, and
-//   reduce-scatters that partial into the owning CTAs' shared memory.  Again
-//   one cluster barrier per step with double-buffered partials.
+//   reduce-scatters that partial into the owning CTAs' shared memory the same
+//   way (double-buffered partials, one mbarrier per buffer).
+// * The recurrent products use packed FP32 FMA (FFMA2) on pairs of
+//   independent partial sums.
 // * Per-step inputs (input gates; dout and the stash) are prefetched `pd`
 //   steps ahead into a shared-memory ring with cp.async.
+// * Every wait is bounded (about 2 s of %globaltimer); on expiry the kernel
+//   records GRU_STATUS_WAIT_TIMEOUT in the device status word
+//   (gru_device_status()), leaves its time loop and exits through the final
+//   cluster barrier.
 //
 // Gate math follows custom_gru.py:117-122 / a100_gru_h256_kernels.cu:758-775
 // (forward) and :852-866 (backward).
 
 #include <cooperative_groups.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 #include "../../include/rnn_kernel_b200.h"
@@ -34,25 +44,85 @@ namespace cg = cooperative_groups;
 
 namespace gru {
 
+__device__ int g_device_status = 0;
+
 namespace {
 
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint32_t mapa_u32(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait: false (and the timeout recorded) if the phase did not
+// complete within kWaitLimitNs.
+__device__ __noinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  for (;;) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (global_ns() - t0 > kWaitLimitNs) {
+      atomicOr(&g_device_status, GRU_STATUS_WAIT_TIMEOUT);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void st_async_f32(uint32_t remote_addr, float v, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(remote_addr),
+               "r"(__float_as_uint(v)), "r"(remote_bar)
+               : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
 __device__ __forceinline__ void cp_async4(float* smem_dst, const float* gmem_src) {
-  unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem_src));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(smem_u32(smem_dst)), "l"(gmem_src));
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_dyn(int n) {
-  // n is 1 or 2 (prefetch depth - 1); wait_group needs an immediate.
   if (n >= 2) cp_async_wait<2>();
   else if (n == 1) cp_async_wait<1>();
   else cp_async_wait<0>();
 }
 
 __device__ __forceinline__ float sigmoidf_acc(float v) { return 1.0f / (1.0f + expf(-v)); }
+
+// Parity of the mbarrier phase that carries the data consumed at iteration
+// `it` (>= 1) from a buffer used every other iteration: one buffer is first
+// consumed at it = 1, the other at it = 2, then each every second iteration.
+__device__ __forceinline__ uint32_t phase_parity(int it) { return (uint32_t)((((it + 1) >> 1) - 1) & 1); }
 
 struct FwdArgs {
   const float* G;     // [B,T,3H] input gates (x.W_ih^T + b_ih)
@@ -64,6 +134,8 @@ struct FwdArgs {
   float* stash;       // [B,T,5H] or null
 };
 
+// R = batch rows per GEMV sub-chunk (= rows per cluster when that is <= 8).
+template <int R>
 __global__ void __launch_bounds__(256, 1)
 gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
   cg::cluster_group cluster = cg::this_cluster();
@@ -76,34 +148,48 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
   const int warp = tid >> 5, lane = tid & 31;
   const int H = g.H, T = g.T, Hc = g.Hc, Kp = g.nw * 32, bcp = g.bcp, pd = g.pd;
   const int j0 = c * Hc;
-  const int hcnt = max(0, min(Hc, H - j0));
+  const int hcnt = max(1, min(Hc, H - j0));
 
   extern __shared__ __align__(16) float smem[];
-  float* hbuf = smem;                              // [2][bcp][Kp]
-  float* part = hbuf + 2 * bcp * Kp;               // [nw][kSub][3][32]
-  float* ring = part + g.nw * kSub * 3 * 32;       // [pd][bcp][3][Hc]
+  __shared__ __align__(8) unsigned long long mbar[2];
+  float* hbuf = smem;                          // [2][bcp][Kp]
+  float* part = smem + g.off1;                 // [nw][R][3][32]
+  float* ring = smem + g.off2;                 // [pd][bcp][3][Hc]
   const int ring_stride = bcp * 3 * Hc;
+  const int slot_stride = bcp * Kp;
 
-  // W_hh rows (r, z, n) of unit j0+lane, columns [32*warp, 32*warp+32).
-  float wr[32], wz[32], wn[32];
+  // W_hh rows (r, z, n) of unit j0+lane, columns [32*warp, 32*warp+32), as
+  // pairs of consecutive columns for FFMA2.
+  float2 wr[16], wz[16], wn[16];
   {
     const int jg = j0 + lane;
-    const bool jv = lane < hcnt;
+    const bool jv = lane < hcnt && jg < H;
 #pragma unroll
-    for (int kk = 0; kk < 32; ++kk) {
-      const int k = warp * 32 + kk;
-      const bool v = jv && k < H;
-      wr[kk] = v ? a.w_hh[(size_t)jg * H + k] : 0.0f;
-      wz[kk] = v ? a.w_hh[(size_t)(H + jg) * H + k] : 0.0f;
-      wn[kk] = v ? a.w_hh[(size_t)(2 * H + jg) * H + k] : 0.0f;
+    for (int kk = 0; kk < 16; ++kk) {
+      const int k = warp * 32 + 2 * kk;
+      const bool v0 = jv && k < H, v1 = jv && k + 1 < H;
+      wr[kk] = make_float2(v0 ? a.w_hh[(size_t)jg * H + k] : 0.f, v1 ? a.w_hh[(size_t)jg * H + k + 1] : 0.f);
+      wz[kk] = make_float2(v0 ? a.w_hh[(size_t)(H + jg) * H + k] : 0.f,
+                           v1 ? a.w_hh[(size_t)(H + jg) * H + k + 1] : 0.f);
+      wn[kk] = make_float2(v0 ? a.w_hh[(size_t)(2 * H + jg) * H + k] : 0.f,
+                           v1 ? a.w_hh[(size_t)(2 * H + jg) * H + k + 1] : 0.f);
     }
   }
 
-  for (int e = tid; e < 2 * bcp * Kp; e += nthr) hbuf[e] = 0.0f;
+  for (int e = tid; e < 2 * slot_stride; e += nthr) hbuf[e] = 0.0f;
+  for (int e = tid; e < g.nw * R * 3 * 32; e += nthr) part[e] = 0.0f;
   __syncthreads();
   for (int e = tid; e < nb * H; e += nthr) {
     const int b = e / H, k = e - b * H;
     hbuf[b * Kp + k] = a.h0[(size_t)(b_begin + b) * H + k];
+  }
+  const uint32_t bar0 = smem_u32(&mbar[0]);
+  const uint32_t bytes_per_step = (uint32_t)(nb * H * 4);
+  if (tid == 0) {
+    mbar_init(bar0, 1);
+    mbar_init(bar0 + 8, 1);
+    fence_mbar_init();
+    if (T > 1) mbar_expect_tx(bar0 + 8, bytes_per_step);  // slot 1 <- step 1
   }
 
   auto issue = [&](int s) {
@@ -123,54 +209,58 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
     else cp_async_commit();
   }
 
-  cluster.sync();  // h buffers of every CTA initialised before any remote write
+  const uint32_t hbuf_u32 = smem_u32(hbuf);
+  cluster.sync();  // buffers and mbarriers of every CTA initialised
 
+  bool ok = true;
   for (int t = 0; t < T; ++t) {
+    const int cur = t & 1, nxt = cur ^ 1;
+    const float* hcur = hbuf + cur * slot_stride;
+    const float* rg = ring + (t % pd) * ring_stride;
+    if (t > 0) ok = mbar_wait_bounded(bar0 + 8 * cur, phase_parity(t));
+    if (!ok) break;
+    // Past the wait every thread of the cluster has sent its step t-1 h
+    // values, and each of those depended on that thread's reads of ring slot
+    // (t-1) % pd, which this prefetch overwrites.
     if (t + pd - 1 < T) issue(t + pd - 1);
     else cp_async_commit();
-    const int cur = t & 1, nxt = cur ^ 1;
-    const float* hcur = hbuf + cur * bcp * Kp;
-    const float* rg = ring + (t % pd) * ring_stride;
 
-    for (int b0 = 0; b0 < nb; b0 += kSub) {
-      float acc[kSub][3];
+    for (int b0 = 0; b0 < nb; b0 += R) {
+      float2 acc[R][3];
 #pragma unroll
-      for (int s = 0; s < kSub; ++s) acc[s][0] = acc[s][1] = acc[s][2] = 0.0f;
+      for (int s = 0; s < R; ++s) acc[s][0] = acc[s][1] = acc[s][2] = make_float2(0.f, 0.f);
       const float* hb = hcur + b0 * Kp + warp * 32;
 #pragma unroll
       for (int kk = 0; kk < 32; kk += 4) {
 #pragma unroll
-        for (int s = 0; s < kSub; ++s) {
+        for (int s = 0; s < R; ++s) {
           const float4 hv = *reinterpret_cast<const float4*>(hb + s * Kp + kk);
-          acc[s][0] = fmaf(wr[kk], hv.x, acc[s][0]);
-          acc[s][1] = fmaf(wz[kk], hv.x, acc[s][1]);
-          acc[s][2] = fmaf(wn[kk], hv.x, acc[s][2]);
-          acc[s][0] = fmaf(wr[kk + 1], hv.y, acc[s][0]);
-          acc[s][1] = fmaf(wz[kk + 1], hv.y, acc[s][1]);
-          acc[s][2] = fmaf(wn[kk + 1], hv.y, acc[s][2]);
-          acc[s][0] = fmaf(wr[kk + 2], hv.z, acc[s][0]);
-          acc[s][1] = fmaf(wz[kk + 2], hv.z, acc[s][1]);
-          acc[s][2] = fmaf(wn[kk + 2], hv.z, acc[s][2]);
-          acc[s][0] = fmaf(wr[kk + 3], hv.w, acc[s][0]);
-          acc[s][1] = fmaf(wz[kk + 3], hv.w, acc[s][1]);
-          acc[s][2] = fmaf(wn[kk + 3], hv.w, acc[s][2]);
+          const float2 h01 = make_float2(hv.x, hv.y), h23 = make_float2(hv.z, hv.w);
+          acc[s][0] = __ffma2_rn(wr[kk / 2], h01, acc[s][0]);
+          acc[s][1] = __ffma2_rn(wz[kk / 2], h01, acc[s][1]);
+          acc[s][2] = __ffma2_rn(wn[kk / 2], h01, acc[s][2]);
+          acc[s][0] = __ffma2_rn(wr[kk / 2 + 1], h23, acc[s][0]);
+          acc[s][1] = __ffma2_rn(wz[kk / 2 + 1], h23, acc[s][1]);
+          acc[s][2] = __ffma2_rn(wn[kk / 2 + 1], h23, acc[s][2]);
         }
       }
 #pragma unroll
-      for (int s = 0; s < kSub; ++s) {
+      for (int s = 0; s < R; ++s) {
 #pragma unroll
-        for (int q = 0; q < 3; ++q) part[((warp * kSub + s) * 3 + q) * 32 + lane] = acc[s][q];
+        for (int q = 0; q < 3; ++q) part[((warp * R + s) * 3 + q) * 32 + lane] = acc[s][q].x + acc[s][q].y;
       }
       if (b0 == 0) cp_async_wait_dyn(pd - 1);
       __syncthreads();
+      // Every thread is past its wait on slot `cur`: re-arm it for step t+2.
+      if (b0 == 0 && tid == 0 && t + 2 < T) mbar_expect_tx(bar0 + 8 * cur, bytes_per_step);
 
-      const int ns = min(kSub, nb - b0);
+      const int ns = min(R, nb - b0);
       for (int e = tid; e < ns * hcnt; e += nthr) {
         const int s = e / hcnt, jl = e - s * hcnt;
         const int b = b0 + s, j = j0 + jl;
         float ar = 0.0f, az = 0.0f, an = 0.0f;
         for (int w = 0; w < g.nw; ++w) {
-          const float* p = part + ((w * kSub + s) * 3) * 32 + jl;
+          const float* p = part + ((w * R + s) * 3) * 32 + jl;
           ar += p[0];
           az += p[32];
           an += p[64];
@@ -184,6 +274,11 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
         const float n = tanhf(gi[2 * Hc] + r * an);
         const float hp = hcur[b * Kp + j];
         const float hnew = n + z * (hp - n);
+        if (t + 1 < T) {
+          const uint32_t la = hbuf_u32 + 4u * (uint32_t)(nxt * slot_stride + b * Kp + j);
+          const uint32_t lb = bar0 + 8u * nxt;
+          for (int q = 0; q < g.C; ++q) st_async_f32(mapa_u32(la, q), hnew, mapa_u32(lb, q));
+        }
         const size_t row = (size_t)(b_begin + b) * T + t;
         a.out[row * H + j] = hnew;
         if (a.stash != nullptr) {
@@ -195,13 +290,12 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
           st[4 * H] = hp;
         }
         if (t == T - 1) a.hn[(size_t)(b_begin + b) * H + j] = hnew;
-        float* dst = hbuf + nxt * bcp * Kp + b * Kp + j;
-        for (int q = 0; q < g.C; ++q) *cluster.map_shared_rank(dst, q) = hnew;
       }
-      __syncthreads();
+      if (b0 + R < nb) __syncthreads();  // `part` is reused by the next sub-chunk
     }
-    cluster.sync();
   }
+  cp_async_wait<0>();
+  cluster.sync();  // no CTA leaves while a peer may still write into it
 }
 
 struct BwdArgs {
@@ -214,6 +308,7 @@ struct BwdArgs {
   float* dh0;          // [B,H]
 };
 
+template <int R>
 __global__ void __launch_bounds__(256, 1)
 gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
   cg::cluster_group cluster = cg::this_cluster();
@@ -226,30 +321,44 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
   const int warp = tid >> 5, lane = tid & 31;
   const int H = g.H, T = g.T, Hc = g.Hc, bcp = g.bcp, pd = g.pd, C = g.C;
   const int j0 = c * Hc;
-  const int hcnt = max(0, min(Hc, H - j0));
+  const int hcnt = max(1, min(Hc, H - j0));
   const int k = warp * 32 + lane;  // W_hh column this thread owns in the GEMV
 
   extern __shared__ __align__(16) float smem[];
+  __shared__ __align__(8) unsigned long long mbar[2];
   float* red = smem;                           // [2][C][bcp][Hc]
-  float* gz = red + 2 * C * bcp * Hc;          // [bcp][Hc]
-  float* dgs = gz + bcp * Hc;                  // [kSub][3][32]
-  float* ring = dgs + kSub * 3 * 32;           // [pd][bcp][6][Hc]
+  float* gz = smem + g.off1;                   // [bcp][Hc]
+  float* dgs = smem + g.off2;                  // [R][3][32]
+  float* ring = smem + g.off3;                 // [pd][bcp][6][Hc]
   const int ring_stride = bcp * 6 * Hc;
   const int red_slot = C * bcp * Hc;
 
-  // W_hh[g*H + j0 + j][k] for j < Hc.
-  float wr[32], wz[32], wn[32];
+  // W_hh[g*H + j0 + j][k] for j < Hc, as pairs (j, j+1) for FFMA2.
+  float2 wr[16], wz[16], wn[16];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    const bool v = j < hcnt && k < H;
-    wr[j] = v ? a.w_hh[(size_t)(j0 + j) * H + k] : 0.0f;
-    wz[j] = v ? a.w_hh[(size_t)(H + j0 + j) * H + k] : 0.0f;
-    wn[j] = v ? a.w_hh[(size_t)(2 * H + j0 + j) * H + k] : 0.0f;
+  for (int jj = 0; jj < 16; ++jj) {
+    const int j = 2 * jj;
+    const bool v0 = j < hcnt && j0 + j < H && k < H;
+    const bool v1 = j + 1 < hcnt && j0 + j + 1 < H && k < H;
+    wr[jj] = make_float2(v0 ? a.w_hh[(size_t)(j0 + j) * H + k] : 0.f,
+                         v1 ? a.w_hh[(size_t)(j0 + j + 1) * H + k] : 0.f);
+    wz[jj] = make_float2(v0 ? a.w_hh[(size_t)(H + j0 + j) * H + k] : 0.f,
+                         v1 ? a.w_hh[(size_t)(H + j0 + j + 1) * H + k] : 0.f);
+    wn[jj] = make_float2(v0 ? a.w_hh[(size_t)(2 * H + j0 + j) * H + k] : 0.f,
+                         v1 ? a.w_hh[(size_t)(2 * H + j0 + j + 1) * H + k] : 0.f);
   }
 
   for (int e = tid; e < 2 * red_slot; e += nthr) red[e] = 0.0f;
   for (int e = tid; e < bcp * Hc; e += nthr) gz[e] = 0.0f;
-  for (int e = tid; e < kSub * 3 * 32; e += nthr) dgs[e] = 0.0f;
+  for (int e = tid; e < R * 3 * 32; e += nthr) dgs[e] = 0.0f;
+  const uint32_t bar0 = smem_u32(&mbar[0]);
+  const uint32_t bytes_per_step = (uint32_t)(C * nb * hcnt * 4);
+  if (tid == 0) {
+    mbar_init(bar0, 1);
+    mbar_init(bar0 + 8, 1);
+    fence_mbar_init();
+    mbar_expect_tx(bar0, bytes_per_step);  // slot 0 <- partials of iteration 0
+  }
 
   // Ring entry q: 0 dout, 1 r, 2 z, 3 n, 4 hn (= W_hn.h + b_hn), 5 h_prev.
   auto issue = [&](int it) {
@@ -278,20 +387,30 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
 
   const int kown = (k < H) ? k / Hc : 0;
   const int kl = (k < H) ? k - kown * Hc : 0;
+  // This thread's partial for row b of slot s lands in red[s][c][b][kl] of
+  // CTA kown and completes bytes on that CTA's mbarrier s.
+  const uint32_t dst_base = mapa_u32(smem_u32(red) + 4u * (uint32_t)(c * bcp * Hc + kl), kown);
+  const uint32_t dst_bar0 = mapa_u32(bar0, kown);
   cluster.sync();
 
+  bool ok = true;
   for (int it = 0; it < T; ++it) {
     const int t = T - 1 - it;
+    const float* rg = ring + (it % pd) * ring_stride;
+    const int rslot = (it + 1) & 1;  // partials written at iteration it-1
+    const float* rin = red + rslot * red_slot;
+    const int wslot = it & 1;
+    if (it > 0) ok = mbar_wait_bounded(bar0 + 8 * rslot, phase_parity(it));
+    if (!ok) break;
+    // Past the wait every CTA has sent its iteration it-1 partials, which
+    // follow (barrier) its reads of ring slot (it-1) % pd overwritten here.
     if (it + pd - 1 < T) issue(it + pd - 1);
     else cp_async_commit();
-    const float* rg = ring + (it % pd) * ring_stride;
-    const float* rin = red + ((t + 1) & 1) * red_slot;  // partials written at step t+1
-    const int wslot = t & 1;
 
-    for (int b0 = 0; b0 < nb; b0 += kSub) {
+    for (int b0 = 0; b0 < nb; b0 += R) {
       if (b0 == 0) cp_async_wait_dyn(pd - 1);
       __syncthreads();
-      const int ns = min(kSub, nb - b0);
+      const int ns = min(R, nb - b0);
       for (int e = tid; e < ns * hcnt; e += nthr) {
         const int s = e / hcnt, jl = e - s * hcnt;
         const int b = b0 + s, j = j0 + jl;
@@ -312,6 +431,10 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
         const float dhn_gate = dn_pre * r;
         const float dr_pre = dr * r * (1.0f - r);
         const float dz_pre = dz * z * (1.0f - z);
+        dgs[(s * 3 + 0) * 32 + jl] = dr_pre;
+        dgs[(s * 3 + 1) * 32 + jl] = dz_pre;
+        dgs[(s * 3 + 2) * 32 + jl] = dhn_gate;
+        gz[b * Hc + jl] = gg * z;
         const size_t row = (size_t)(b_begin + b) * T + t;
         float* gi = a.dGi + row * 3 * H + j;
         float* gh = a.dGh + row * 3 * H + j;
@@ -321,44 +444,64 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
         gh[0] = dr_pre;
         gh[H] = dz_pre;
         gh[2 * H] = dhn_gate;
-        dgs[(s * 3 + 0) * 32 + jl] = dr_pre;
-        dgs[(s * 3 + 1) * 32 + jl] = dz_pre;
-        dgs[(s * 3 + 2) * 32 + jl] = dhn_gate;
-        gz[b * Hc + jl] = gg * z;
       }
       __syncthreads();
+      // Every thread has consumed slot `rslot`: re-arm it for iteration it+2
+      // (iteration T is the final dh0 read below).
+      if (b0 == 0 && tid == 0 && it > 0 && it + 2 <= T) mbar_expect_tx(bar0 + 8 * rslot, bytes_per_step);
+      if (b0 == 0 && tid == 0 && it == 0 && T >= 2) mbar_expect_tx(bar0 + 8, bytes_per_step);
 
       if (k < H) {
-        float* dst = cluster.map_shared_rank(red + wslot * red_slot + (c * bcp + b0) * Hc + kl, kown);
-#pragma unroll 1
-        for (int s = 0; s < ns; ++s) {
-          const float* d = dgs + s * 3 * 32;
-          float xr = 0.0f, xz = 0.0f, xn = 0.0f;
+        const uint32_t dst = dst_base + 4u * (uint32_t)(wslot * red_slot + b0 * Hc);
+        const uint32_t dbar = dst_bar0 + 8u * wslot;
+        float2 acc[R][3];
 #pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            const float4 vr = *reinterpret_cast<const float4*>(d + j);
-            const float4 vz = *reinterpret_cast<const float4*>(d + 32 + j);
-            const float4 vn = *reinterpret_cast<const float4*>(d + 64 + j);
-            xr = fmaf(vr.x, wr[j], xr); xz = fmaf(vz.x, wz[j], xz); xn = fmaf(vn.x, wn[j], xn);
-            xr = fmaf(vr.y, wr[j + 1], xr); xz = fmaf(vz.y, wz[j + 1], xz); xn = fmaf(vn.y, wn[j + 1], xn);
-            xr = fmaf(vr.z, wr[j + 2], xr); xz = fmaf(vz.z, wz[j + 2], xz); xn = fmaf(vn.z, wn[j + 2], xn);
-            xr = fmaf(vr.w, wr[j + 3], xr); xz = fmaf(vz.w, wz[j + 3], xz); xn = fmaf(vn.w, wn[j + 3], xn);
+        for (int s = 0; s < R; ++s) acc[s][0] = acc[s][1] = acc[s][2] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+#pragma unroll
+          for (int s = 0; s < R; ++s) {
+            const float* d = dgs + s * 3 * 32 + j;
+            const float4 vr = *reinterpret_cast<const float4*>(d);
+            const float4 vz = *reinterpret_cast<const float4*>(d + 32);
+            const float4 vn = *reinterpret_cast<const float4*>(d + 64);
+            acc[s][0] = __ffma2_rn(make_float2(vr.x, vr.y), wr[j / 2], acc[s][0]);
+            acc[s][1] = __ffma2_rn(make_float2(vz.x, vz.y), wz[j / 2], acc[s][1]);
+            acc[s][2] = __ffma2_rn(make_float2(vn.x, vn.y), wn[j / 2], acc[s][2]);
+            acc[s][0] = __ffma2_rn(make_float2(vr.z, vr.w), wr[j / 2 + 1], acc[s][0]);
+            acc[s][1] = __ffma2_rn(make_float2(vz.z, vz.w), wz[j / 2 + 1], acc[s][1]);
+            acc[s][2] = __ffma2_rn(make_float2(vn.z, vn.w), wn[j / 2 + 1], acc[s][2]);
           }
-          dst[s * Hc] = xr + xz + xn;
+        }
+#pragma unroll
+        for (int s = 0; s < R; ++s) {
+          if (s < ns) {
+            const float v = (acc[s][0].x + acc[s][0].y) + (acc[s][1].x + acc[s][1].y) +
+                            (acc[s][2].x + acc[s][2].y);
+            st_async_f32(dst + 4u * (uint32_t)(s * Hc), v, dbar);
+          }
         }
       }
     }
-    cluster.sync();
   }
 
-  // dh0 = direct term of step 0 + every CTA's partial written at step 0.
-  const float* rin = red;  // slot (0 & 1)
-  for (int e = tid; e < nb * hcnt; e += nthr) {
-    const int b = e / hcnt, jl = e - b * hcnt;
-    float dh = gz[b * Hc + jl];
-    for (int q = 0; q < C; ++q) dh += rin[(q * bcp + b) * Hc + jl];
-    a.dh0[(size_t)(b_begin + b) * H + j0 + jl] = dh;
+  // dh0 = g*z of iteration T-1 (t = 0) plus every CTA's partial product of
+  // that iteration, which arrive in slot (T+1)&1.
+  if (ok && T > 0) {
+    const int rslot = (T + 1) & 1;
+    ok = mbar_wait_bounded(bar0 + 8 * rslot, phase_parity(T));
+    if (ok) {
+      const float* rin = red + rslot * red_slot;
+      for (int e = tid; e < nb * hcnt; e += nthr) {
+        const int b = e / hcnt, jl = e - b * hcnt;
+        float dh = gz[b * Hc + jl];
+        for (int q = 0; q < C; ++q) dh += rin[(q * bcp + b) * Hc + jl];
+        a.dh0[(size_t)(b_begin + b) * H + j0 + jl] = dh;
+      }
+    }
   }
+  cp_async_wait<0>();
+  cluster.sync();
 }
 
 int base_geometry(int B, int T, int H, RecGeom* g) {
@@ -371,28 +514,60 @@ int base_geometry(int B, int T, int H, RecGeom* g) {
   return GRU_OK;
 }
 
-size_t fwd_smem(const RecGeom& g) {
+inline int round4(size_t v) { return (int)((v + 3) / 4 * 4); }
+
+// Lay out the forward kernel's shared memory in g (offsets) and return its size.
+size_t fwd_smem(RecGeom& g) {
   const int Kp = g.nw * 32;
-  return sizeof(float) * ((size_t)2 * g.bcp * Kp + (size_t)g.nw * kSub * 3 * 32 +
-                          (size_t)g.pd * g.bcp * 3 * g.Hc);
+  g.off1 = round4((size_t)2 * g.bcp * Kp);
+  g.off2 = g.off1 + round4((size_t)g.nw * g.R * 3 * 32);
+  g.off3 = g.off2 + round4((size_t)g.pd * g.bcp * 3 * g.Hc);
+  return sizeof(float) * (size_t)g.off3;
 }
-size_t bwd_smem(const RecGeom& g) {
-  return sizeof(float) * ((size_t)2 * g.C * g.bcp * g.Hc + (size_t)g.bcp * g.Hc +
-                          (size_t)kSub * 3 * 32 + (size_t)g.pd * g.bcp * 6 * g.Hc);
+size_t bwd_smem(RecGeom& g) {
+  g.off1 = round4((size_t)2 * g.C * g.bcp * g.Hc);
+  g.off2 = g.off1 + round4((size_t)g.bcp * g.Hc);
+  g.off3 = g.off2 + round4((size_t)g.R * 3 * 32);
+  return sizeof(float) * (size_t)(g.off3 + round4((size_t)g.pd * g.bcp * 6 * g.Hc));
+}
+
+template <int R>
+const void* fwd_kernel_ptr() { return (const void*)gru_fwd_recurrent_kernel<R>; }
+template <int R>
+const void* bwd_kernel_ptr() { return (const void*)gru_bwd_recurrent_kernel<R>; }
+
+const void* kernel_for(bool fwd, int R) {
+  switch (R) {
+#define GRU_CASE(r) \
+  case r: return fwd ? fwd_kernel_ptr<r>() : bwd_kernel_ptr<r>();
+    GRU_CASE(1) GRU_CASE(2) GRU_CASE(3) GRU_CASE(4) GRU_CASE(5) GRU_CASE(6) GRU_CASE(7) GRU_CASE(8)
+#undef GRU_CASE
+    default: return nullptr;
+  }
 }
 
 // Choose the batch rows per cluster: spread B over as many clusters as can be
 // resident at once, subject to the shared-memory budget.
 template <typename SmemFn>
-int finish_geometry(RecGeom* g, int device, const void* kernel, SmemFn smem_of) {
-  int max_smem = 0;
-  GRU_CUDA_TRY(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
-  GRU_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem));
+int finish_geometry(RecGeom* g, int device, bool fwd, SmemFn smem_of) {
+  static_assert(sizeof(float) == 4, "layout assumes 4-byte floats");
+  int optin = 0;
+  GRU_CUDA_TRY(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+  int max_smem = optin;  // dynamic budget = opt-in limit minus the kernel's static shared memory
+  for (int r = 1; r <= kMaxRows; ++r) {
+    cudaFuncAttributes fa{};
+    GRU_CUDA_TRY(cudaFuncGetAttributes(&fa, kernel_for(fwd, r)));
+    max_smem = std::min(max_smem, optin - (int)fa.sharedSizeBytes);
+  }
+  for (int r = 1; r <= kMaxRows; ++r)
+    GRU_CUDA_TRY(cudaFuncSetAttribute(kernel_for(fwd, r), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      max_smem));
 
-  // Probe cluster residency with a small configuration.
+  // Cluster residency probe with a small configuration.
   g->pd = 3;
-  g->bc = kSub;
-  g->bcp = kSub;
+  g->R = kMaxRows;
+  g->bc = kMaxRows;
+  g->bcp = kMaxRows;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(g->C, 1, 1);
   cfg.blockDim = dim3(32 * g->nw, 1, 1);
@@ -405,7 +580,7 @@ int finish_geometry(RecGeom* g, int device, const void* kernel, SmemFn smem_of) 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int max_clusters = 0;
-  GRU_CUDA_TRY(cudaOccupancyMaxActiveClusters(&max_clusters, kernel, &cfg));
+  GRU_CUDA_TRY(cudaOccupancyMaxActiveClusters(&max_clusters, kernel_for(fwd, kMaxRows), &cfg));
   if (max_clusters < 1) {
     set_error("no cluster of the recurrent kernel fits on this device");
     return GRU_ERR_UNSUPPORTED;
@@ -413,7 +588,8 @@ int finish_geometry(RecGeom* g, int device, const void* kernel, SmemFn smem_of) 
   int bc = ceil_div(g->B, max_clusters);
   for (;;) {
     g->bc = bc;
-    g->bcp = ceil_div(bc, kSub) * kSub;
+    g->R = bc < kMaxRows ? bc : kMaxRows;
+    g->bcp = ceil_div(bc, g->R) * g->R;
     g->pd = 3;
     if (smem_of(*g) > (size_t)max_smem) g->pd = 2;
     if (smem_of(*g) <= (size_t)max_smem) break;
@@ -421,16 +597,20 @@ int finish_geometry(RecGeom* g, int device, const void* kernel, SmemFn smem_of) 
       set_error("recurrent kernel shared memory does not fit");
       return GRU_ERR_UNSUPPORTED;
     }
-    bc = bc > kSub ? bc - kSub : bc - 1;
+    bc = bc > kMaxRows ? bc - kMaxRows : bc - 1;
   }
   g->nclusters = ceil_div(g->B, g->bc);
   g->smem = smem_of(*g);
+  if ((g->off1 | g->off2 | g->off3) & 3) {
+    set_error("internal: recurrent shared-memory region not 16-byte aligned");
+    return GRU_ERR_INVALID;
+  }
+  g->max_clusters = max_clusters;
   return GRU_OK;
 }
 
 template <typename Args>
-int launch_clusters(void (*kernel)(Args, RecGeom), const Args& a, const RecGeom& g,
-                    cudaStream_t stream, int kind) {
+int launch_clusters(const void* kernel, const Args& a, const RecGeom& g, cudaStream_t stream, int kind) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(g.C * g.nclusters, 1, 1);
   cfg.blockDim = dim3(32 * g.nw, 1, 1);
@@ -443,35 +623,48 @@ int launch_clusters(void (*kernel)(Args, RecGeom), const Args& a, const RecGeom&
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  Args args = a;
+  RecGeom geom = g;
+  void* params[2] = {&args, &geom};
   LaunchScope scope(kind, stream);
-  GRU_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, a, g));
+  GRU_CUDA_TRY(cudaLaunchKernelExC(&cfg, kernel, params));
   return GRU_OK;
 }
 
 }  // namespace
 
+int read_device_status(int reset, int* status) {
+  GRU_CUDA_TRY(cudaDeviceSynchronize());
+  GRU_CUDA_TRY(cudaMemcpyFromSymbol(status, g_device_status, sizeof(int)));
+  if (reset) {
+    const int zero = 0;
+    GRU_CUDA_TRY(cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int)));
+  }
+  return GRU_OK;
+}
+
 int rec_forward_geometry(int B, int T, int H, int device, RecGeom* g) {
   base_geometry(B, T, H, g);
-  return finish_geometry(g, device, (const void*)gru_fwd_recurrent_kernel, fwd_smem);
+  return finish_geometry(g, device, true, fwd_smem);
 }
 
 int rec_backward_geometry(int B, int T, int H, int device, RecGeom* g) {
   base_geometry(B, T, H, g);
-  return finish_geometry(g, device, (const void*)gru_bwd_recurrent_kernel, bwd_smem);
+  return finish_geometry(g, device, false, bwd_smem);
 }
 
 int launch_rec_forward(const float* G, const float* h0, const float* w_hh, const float* b_hh,
                        float* out, float* hn, float* stash, const RecGeom& g,
                        cudaStream_t stream) {
   FwdArgs a{G, h0, w_hh, b_hh, out, hn, stash};
-  return launch_clusters(gru_fwd_recurrent_kernel, a, g, stream, kKindFwdRecurrent);
+  return launch_clusters(kernel_for(true, g.R), a, g, stream, kKindFwdRecurrent);
 }
 
 int launch_rec_backward(const float* dout, const float* dhn, const float* w_hh,
                         const float* stash, float* dGi, float* dGh, float* dh0,
                         const RecGeom& g, cudaStream_t stream) {
   BwdArgs a{dout, dhn, w_hh, stash, dGi, dGh, dh0};
-  return launch_clusters(gru_bwd_recurrent_kernel, a, g, stream, kKindBwdRecurrent);
+  return launch_clusters(kernel_for(false, g.R), a, g, stream, kKindBwdRecurrent);
 }
 
 }  // namespace gru

@@ -1,7 +1,24 @@
-"""Shared parity harness for the GPU tests: run torch.nn.GRU FP32 on the CPU
-(the reference's parity anchor, tests/test_a100_prod.py:84-126) and the B200
-module on cuda:0 on the same seeded inputs, and compare every output and
-gradient within the north-star tolerance rtol 1e-4 / atol 1e-5."""
+"""Shared parity harness for the GPU tests.
+
+Runs torch.nn.GRU on the CPU in FP32 (the reference's parity anchor,
+tests/test_a100_prod.py:84-126) and in FP64 (the truth), and the B200 module on
+cuda:0, on the same seeded inputs; then checks every output and gradient:
+
+* against the FP64 truth at the north-star tolerance rtol 1e-4 / atol 1e-5,
+  element-wise, with no slack;
+* against torch FP32 at the same tolerance plus torch FP32's own measured
+  deviation from the truth, element-wise (that term is ~0 except on weight
+  gradients, see below).
+
+Stress cases drive the backward with unit-scale random upstream gradients
+instead of the BASELINE losses.  There every weight gradient is a sum of
+B*T ~ 1e4-1e5 terms of size ~1, and the FP32 rounding of the forward
+activations alone moves some of its entries by more than 1e-5 + 1e-4*|value|
+from the FP64 truth: torch FP32 itself misses the element-wise bar by up to 8x
+at BASELINE config 2.  For those tensors ``weights="envelope"`` requires the
+result to be at least as close to the truth as torch FP32 is (max and RMS
+error within 1.25x of torch's, plus atol); every other tensor stays strict.
+"""
 from __future__ import annotations
 
 import torch
@@ -11,7 +28,8 @@ from rnn_kernel_b200 import from_torch_gru
 RTOL, ATOL = 1e-4, 1e-5
 
 
-def run_pair(I, H, L, B, T, seed, loss="random", h0_scale=1.0, ref_dtype=torch.float32):
+def run_pair(I, H, L, B, T, seed, loss="random", h0_scale=1.0, ref_dtype=torch.float32, truth=True):
+    """Returns (ours, torch_fp32, torch_fp64 or None)."""
     torch.manual_seed(seed)
     ref = torch.nn.GRU(I, H, num_layers=L, batch_first=True)
     x = torch.randn(B, T, I)
@@ -21,8 +39,8 @@ def run_pair(I, H, L, B, T, seed, loss="random", h0_scale=1.0, ref_dtype=torch.f
     tgt = torch.randn(B, T, H)
 
     def run(model, dev, dtype):
-        xx = x.to(dev, dtype).requires_grad_(True)
-        hh = h0.to(dev, dtype).requires_grad_(True)
+        xx = x.detach().clone().to(dev, dtype).requires_grad_(True)
+        hh = h0.detach().clone().to(dev, dtype).requires_grad_(True)
         out, hn = model(xx, hh)
         if loss == "random":
             torch.autograd.backward([out, hn], [go.to(dev, dtype), gh.to(dev, dtype)])
@@ -39,20 +57,43 @@ def run_pair(I, H, L, B, T, seed, loss="random", h0_scale=1.0, ref_dtype=torch.f
             res["d" + n] = p.grad
         return {k: v.detach().double().cpu() for k, v in res.items()}
 
-    ours = from_torch_gru(ref.cuda())
+    import copy
+
+    ours = from_torch_gru(copy.deepcopy(ref).cuda())
     mine = run(ours, "cuda", torch.float32)
-    ref_cpu = ref.cpu().to(ref_dtype)
-    theirs = run(ref_cpu, "cpu", ref_dtype)
-    return mine, theirs
+    theirs = run(copy.deepcopy(ref).to(ref_dtype), "cpu", ref_dtype)
+    t64 = run(copy.deepcopy(ref).double(), "cpu", torch.float64) if truth else None
+    return mine, theirs, t64
 
 
-def assert_parity(mine, theirs, rtol=RTOL, atol=ATOL):
+def _envelope_ok(a, t32, t64, atol):
+    e_ours = (a - t64).abs()
+    e_ref = (t32 - t64).abs()
+    rms = lambda e: float(e.pow(2).mean().sqrt())
+    return (float(e_ours.max()) <= 1.25 * float(e_ref.max()) + atol
+            and rms(e_ours) <= 1.25 * rms(e_ref) + atol), float(e_ours.max()), float(e_ref.max())
+
+
+def assert_parity(mine, t32, t64=None, rtol=RTOL, atol=ATOL, weights="strict"):
     bad = []
-    for k in theirs:
-        a, b = mine[k], theirs[k]
+    for k in t32:
+        if weights == "envelope" and k.startswith("dweight") and t64 is not None:
+            ok, eo, er = _envelope_ok(mine[k], t32[k], t64[k], atol)
+            if not ok:
+                bad.append(f"{k}: error vs fp64 truth {eo:.3e} exceeds torch fp32's {er:.3e} (x1.25)")
+            continue
+        a, b = mine[k], t32[k]
         assert a.shape == b.shape, (k, a.shape, b.shape)
-        if not torch.allclose(a, b, rtol=rtol, atol=atol):
-            err = (a - b).abs()
-            lim = atol + rtol * b.abs()
-            bad.append(f"{k}: max|d|={err.max():.3e} worst ratio={(err / lim).max():.2f} max|ref|={b.abs().max():.3e}")
+        slack = (t32[k] - t64[k]).abs() if t64 is not None else 0.0
+        lim = atol + rtol * b.abs() + slack
+        err = (a - b).abs()
+        if bool((err > lim).any()):
+            bad.append(f"{k} vs torch32(+own err): max|d|={err.max():.3e} worst ratio={(err / lim).max():.2f}")
+        if t64 is not None:
+            c = t64[k]
+            err = (a - c).abs()
+            lim = atol + rtol * c.abs()
+            if bool((err > lim).any()):
+                bad.append(f"{k} vs fp64 truth: max|d|={err.max():.3e} worst ratio={(err / lim).max():.2f} "
+                           f"max|ref|={c.abs().max():.3e}")
     assert not bad, "\n".join(bad)

@@ -31,10 +31,10 @@ def test_golden_fixtures(case):
     got = {"out": out, "hn": hn, "dx": x.grad, "dh0": h0.grad}
     for n, p in m.named_parameters():
         got["d" + n] = p.grad
-    for k, v in got.items():
-        v = v.detach().double().cpu().numpy()
-        np.testing.assert_allclose(v, d[f"custom64_{k}"], rtol=RTOL, atol=ATOL, err_msg=f"{k} vs CustomGRU fp64")
-        np.testing.assert_allclose(v, d[f"torch32_{k}"], rtol=RTOL, atol=ATOL, err_msg=f"{k} vs nn.GRU fp32")
+    mine = {k: v.detach().double().cpu() for k, v in got.items()}
+    t32 = {k: torch.from_numpy(d[f"torch32_{k}"]).double() for k in got}
+    t64 = {k: torch.from_numpy(d[f"custom64_{k}"]) for k in got}
+    assert_parity(mine, t32, t64)
 
 
 @pytest.mark.parametrize("I,H,L,B,T", [
@@ -42,44 +42,52 @@ def test_golden_fixtures(case):
     (16, 256, 4, 2, 5), (3, 31, 1, 5, 3), (9, 64, 3, 4, 9), (300, 40, 1, 2, 4),
 ])
 def test_small_shapes(I, H, L, B, T):
-    mine, theirs = run_pair(I, H, L, B, T, seed=1000 + 10 * L + I + H)
-    assert_parity(mine, theirs)
+    mine, theirs, truth = run_pair(I, H, L, B, T, seed=1000 + 10 * L + I + H)
+    assert_parity(mine, theirs, truth)
 
 
 @pytest.mark.parametrize("H", [64, 96, 128, 129, 130, 160, 192, 256])
 def test_hidden_sweep_config3(H):
-    # input_size=H, batch=64, seq_len=256, seed = H.
-    mine, theirs = run_pair(H, H, 1, 64, 256, seed=H)
-    assert_parity(mine, theirs)
+    # input_size=H, batch=64, seq_len=256, seed = H, MSE loss.
+    mine, theirs, truth = run_pair(H, H, 1, 64, 256, seed=H, loss="mse", h0_scale=0)
+    assert_parity(mine, theirs, truth)
+
+
+@pytest.mark.parametrize("H", [64, 129, 130, 256])
+def test_hidden_sweep_unit_grads(H):
+    # Config-3 shapes driven by unit-scale random upstream gradients (stress).
+    mine, theirs, truth = run_pair(H, H, 1, 64, 256, seed=H)
+    assert_parity(mine, theirs, truth, weights="envelope")
 
 
 def test_prod_shape_config2():
     # I=H=256, B=64, T=512, h0=0, MSE against N(0,1) target.
-    mine, theirs = run_pair(256, 256, 1, 64, 512, seed=2, loss="mse", h0_scale=0)
-    assert_parity(mine, theirs)
+    mine, theirs, truth = run_pair(256, 256, 1, 64, 512, seed=2, loss="mse", h0_scale=0)
+    assert_parity(mine, theirs, truth)
 
 
 def test_prod_shape_random_grads():
     # Same shape, unit-scale upstream gradients (much larger dW than the MSE case).
-    mine, theirs = run_pair(256, 256, 1, 64, 512, seed=3)
-    assert_parity(mine, theirs)
+    mine, theirs, truth = run_pair(256, 256, 1, 64, 512, seed=3)
+    assert_parity(mine, theirs, truth, weights="envelope")
 
 
 def test_stacked_config4():
     # 2 layers, I=128, H=256, B=128, T=1024, h0 ~ 0.1*N(0,1), loss sum(out^2).
-    mine, theirs = run_pair(128, 256, 2, 128, 1024, seed=4, loss="sumsq", h0_scale=0.1)
-    assert_parity(mine, theirs)
+    mine, theirs, truth = run_pair(128, 256, 2, 128, 1024, seed=4, loss="sumsq", h0_scale=0.1)
+    # d(sum out^2)/d out = 2*out is unit-scale: weight gradients use the envelope check.
+    assert_parity(mine, theirs, truth, weights="envelope")
 
 
 @pytest.mark.parametrize("B,T", [(257, 6), (1100, 3), (3000, 2)])
 def test_large_batch_many_clusters(B, T):
-    mine, theirs = run_pair(8, 64, 1, B, T, seed=B)
-    assert_parity(mine, theirs)
+    mine, theirs, truth = run_pair(8, 64, 1, B, T, seed=B)
+    assert_parity(mine, theirs, truth, weights="envelope")
 
 
 def test_hn_only_loss_grad_output_none():
-    mine, theirs = run_pair(6, 48, 2, 3, 7, seed=5, loss="hn_only")
-    assert_parity(mine, theirs)
+    mine, theirs, truth = run_pair(6, 48, 2, 3, 7, seed=5, loss="hn_only")
+    assert_parity(mine, theirs, truth)
 
 
 @pytest.mark.parametrize("L", [1, 2, 3])
@@ -134,9 +142,9 @@ def test_empty_batch_and_sequence():
 
 def test_native_library_is_what_runs():
     before = _lib.launch_count()
-    mine, theirs = run_pair(4, 32, 1, 2, 3, seed=7)
+    mine, theirs, truth = run_pair(4, 32, 1, 2, 3, seed=7)
     assert _lib.launch_count() > before
-    assert_parity(mine, theirs)
+    assert_parity(mine, theirs, truth)
 
 
 def test_rejects_bad_inputs_on_gpu():
