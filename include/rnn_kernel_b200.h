@@ -80,8 +80,9 @@ int gru_backward(const float* dout, const float* dhn, const float* x, const floa
 /* ---- Telemetry (no reference counterpart: the reference had no kernel
  * timers; its profiling scripts used torch.profiler / nsys, see
  * scripts/profile_a100_h256_step.py).  Kernel kinds: 0 input-projection GEMM,
- * 1 forward time loop, 2 backward time loop, 3 gradient GEMMs (+ split-K
- * reduce), 4 bias-gradient column sums. ---- */
+ * 1 forward time loop, 2 backward time loop, 3 gradient products (dW, dx;
+ * + split-K reduce), 4 bias-gradient column sums, 5 padding / transpose
+ * copies. ---- */
 
 /* Device status word of the current device: 0 when every kernel so far ran
  * to completion, else GRU_STATUS_* bits (a bounded wait inside a time-loop

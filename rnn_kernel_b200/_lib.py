@@ -34,7 +34,7 @@ SIGNATURES = {
     "gru_timing_collect": (_int, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int), _int]),
 }
 
-KERNEL_KINDS = ("input_gemm", "fwd_recurrent", "bwd_recurrent", "grad_gemm", "colsum")
+KERNEL_KINDS = ("input_gemm", "fwd_recurrent", "bwd_recurrent", "grad_gemm", "colsum", "layout")
 
 
 def timing_enable(on: bool) -> None:

@@ -50,7 +50,7 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
         return LIB_PATH
     tmp = LIB_PATH.with_suffix(".so.tmp")
     cmd = [nvcc_path(), *NVCC_FLAGS, *(extra or []), "-I", str(ROOT / "include"),
-           *map(str, sources()), "-o", str(tmp), "-lcuda"]
+           *map(str, sources()), "-o", str(tmp)]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
     subprocess.run(cmd, check=True)

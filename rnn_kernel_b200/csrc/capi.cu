@@ -64,22 +64,49 @@ int current_device(int* dev) {
   return GRU_OK;
 }
 
+inline int pad4(int v) { return (v + 3) / 4 * 4; }
+
+struct FwdLayout {
+  size_t g, xp, wp, total;
+  bool pad;  // x / W_ih need a copy with a 16-byte row stride for TMA
+};
+
+FwdLayout fwd_layout(int B, int T, int I, int H) {
+  const long BT = (long)B * T;
+  FwdLayout l{};
+  l.pad = (I % 4) != 0;
+  size_t off = 0;
+  l.g = off;
+  off = align_up(off + sizeof(float) * BT * 3 * H, kAlign);
+  if (l.pad) {
+    l.xp = off;
+    off = align_up(off + sizeof(float) * BT * pad4(I), kAlign);
+    l.wp = off;
+    off = align_up(off + sizeof(float) * (size_t)3 * H * pad4(I), kAlign);
+  }
+  l.total = off;
+  return l;
+}
+
 struct BwdLayout {
-  size_t dgi, dgh, gemm, col, total;
+  size_t dgi, dgh, wt, gemm, col, total;
+  int ldgi;  // row stride of dG_ih (multiple of 4 floats for TMA)
 };
 
 BwdLayout bwd_layout(int B, int T, int I, int H, int device) {
   const long BT = (long)B * T;
   BwdLayout l{};
+  l.ldgi = pad4(3 * H);
   size_t off = 0;
   l.dgi = off;
-  off = align_up(off + sizeof(float) * BT * 3 * H, kAlign);
+  off = align_up(off + sizeof(float) * BT * l.ldgi, kAlign);
   l.dgh = off;
   off = align_up(off + sizeof(float) * BT * 3 * H, kAlign);
+  l.wt = off;
+  off = align_up(off + sizeof(float) * (size_t)I * l.ldgi, kAlign);
   l.gemm = off;
   size_t g = gemm_ws_bytes(3 * H, H, (int)BT, device);
   g = std::max(g, gemm_ws_bytes(3 * H, I, (int)BT, device));
-  g = std::max(g, gemm_ws_bytes((int)BT, I, 3 * H, device));
   off = align_up(off + g, kAlign);
   l.col = off;
   off = align_up(off + colsum_ws_bytes(BT, 3 * H), kAlign);
@@ -126,9 +153,10 @@ int gru_device_supported(int device) {
 
 int gru_device_status(int reset) {
   clear_error();
-  int st = 0;
+  int st = 0, st2 = 0;
   if (read_device_status(reset, &st) != GRU_OK) return -1;
-  return st;
+  if (read_gemm_status(reset, &st2) != GRU_OK) return -1;
+  return st | st2;
 }
 
 size_t gru_stash_bytes(int B, int T, int H) {
@@ -137,9 +165,8 @@ size_t gru_stash_bytes(int B, int T, int H) {
 }
 
 size_t gru_forward_workspace_bytes(int B, int T, int I, int H) {
-  if (B <= 0 || T <= 0 || H <= 0) return 0;
-  (void)I;
-  return align_up(sizeof(float) * (size_t)B * T * 3 * H, kAlign);
+  if (B <= 0 || T <= 0 || H <= 0 || I <= 0) return 0;
+  return fwd_layout(B, T, I, H).total;
 }
 
 size_t gru_backward_workspace_bytes(int B, int T, int I, int H) {
@@ -175,9 +202,26 @@ int gru_forward(const float* x, const float* h0, const float* w_ih, const float*
     set_error("gru_forward: workspace too small");
     return GRU_ERR_INVALID;
   }
-  float* G = static_cast<float*>(workspace);
-  GemmArgs ga{x, I, 1, w_ih, 1, I, G, 3 * H, b_ih, B * T, 3 * H, I};
-  if ((rc = gemm(ga, nullptr, 0, dev, stream, kKindInputGemm))) return rc;
+  const FwdLayout l = fwd_layout(B, T, I, H);
+  char* ws = static_cast<char*>(workspace);
+  float* G = reinterpret_cast<float*>(ws + l.g);
+  // G = x . W_ih^T + b_ih on the tensor cores (3xTF32).
+  TcGemmArgs ga{x, I, w_ih, I, G, 3 * H, b_ih, B * T, 3 * H, I};
+  if (l.pad || !tc_gemm_supported(ga)) {
+    if (!l.pad) {
+      set_error("gru_forward: x and w_ih must be 16-byte aligned");
+      return GRU_ERR_INVALID;
+    }
+    float* xp = reinterpret_cast<float*>(ws + l.xp);
+    float* wp = reinterpret_cast<float*>(ws + l.wp);
+    if ((rc = pad_rows(x, (long)B * T, I, xp, pad4(I), stream))) return rc;
+    if ((rc = pad_rows(w_ih, 3L * H, I, wp, pad4(I), stream))) return rc;
+    ga.A = xp;
+    ga.lda = pad4(I);
+    ga.B = wp;
+    ga.ldb = pad4(I);
+  }
+  if ((rc = tc_gemm(ga, stream, kKindInputGemm))) return rc;
   RecGeom g{};
   if ((rc = geometry(0, B, T, H, dev, &g))) return rc;
   return launch_rec_forward(G, h0, w_hh, b_hh, out, hn, stash, g, stream);
@@ -222,9 +266,10 @@ int gru_backward(const float* dout, const float* dhn, const float* x, const floa
   float* dGh = reinterpret_cast<float*>(ws + l.dgh);
   void* gws = ws + l.gemm;
   const size_t gws_bytes = l.col - l.gemm;
+  float* wt = reinterpret_cast<float*>(ws + l.wt);
   RecGeom g{};
   if ((rc = geometry(1, B, T, H, dev, &g))) return rc;
-  if ((rc = launch_rec_backward(dout, dhn, w_hh, stash, dGi, dGh, dh0, g, stream))) return rc;
+  if ((rc = launch_rec_backward(dout, dhn, w_hh, stash, dGi, l.ldgi, dGh, dh0, g, stream))) return rc;
 
   const int BT = B * T;
   const int H3 = 3 * H;
@@ -232,15 +277,16 @@ int gru_backward(const float* dout, const float* dhn, const float* x, const floa
   GemmArgs a1{dGh, 1, H3, stash + 4 * H, 5L * H, 1, dw_hh, H, nullptr, H3, H, BT};
   if ((rc = gemm(a1, gws, gws_bytes, dev, stream, kKindGradGemm, true))) return rc;
   // dW_ih = dG_ih^T . x
-  GemmArgs a2{dGi, 1, H3, x, I, 1, dw_ih, I, nullptr, H3, I, BT};
+  GemmArgs a2{dGi, 1, l.ldgi, x, I, 1, dw_ih, I, nullptr, H3, I, BT};
   if ((rc = gemm(a2, gws, gws_bytes, dev, stream, kKindGradGemm, true))) return rc;
   if (dx) {
-    // dx = dG_ih . W_ih
-    GemmArgs a3{dGi, H3, 1, w_ih, I, 1, dx, I, nullptr, BT, I, H3};
-    if ((rc = gemm(a3, gws, gws_bytes, dev, stream, kKindGradGemm))) return rc;
+    // dx = dG_ih . W_ih on the tensor cores, with W_ih^T staged as [I, ldgi].
+    if ((rc = transpose(w_ih, H3, I, wt, l.ldgi, stream))) return rc;
+    TcGemmArgs a3{dGi, l.ldgi, wt, l.ldgi, dx, I, nullptr, BT, I, H3};
+    if ((rc = tc_gemm(a3, stream, kKindGradGemm))) return rc;
   }
-  if ((rc = colsum(dGi, BT, H3, db_ih, ws + l.col, stream))) return rc;
-  if ((rc = colsum(dGh, BT, H3, db_hh, ws + l.col, stream))) return rc;
+  if ((rc = colsum(dGi, BT, H3, l.ldgi, db_ih, ws + l.col, stream))) return rc;
+  if ((rc = colsum(dGh, BT, H3, H3, db_hh, ws + l.col, stream))) return rc;
   return GRU_OK;
 }
 

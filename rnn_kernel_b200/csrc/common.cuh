@@ -59,7 +59,7 @@ int launch_rec_forward(const float* G, const float* h0, const float* w_hh, const
                        float* out, float* hn, float* stash, const RecGeom& g,
                        cudaStream_t stream);
 int launch_rec_backward(const float* dout, const float* dhn, const float* w_hh,
-                        const float* stash, float* dGi, float* dGh, float* dh0,
+                        const float* stash, float* dGi, int ldgi, float* dGh, float* dh0,
                         const RecGeom& g, cudaStream_t stream);
 
 // ---------------------------------------------------------------------------
@@ -80,10 +80,30 @@ size_t gemm_ws_bytes(int M, int N, int K, int device);
 int gemm(const GemmArgs& a, void* ws, size_t ws_bytes, int device, cudaStream_t stream, int kind,
          bool exact = false);
 
-// Column sums of a row-major [rows, cols] matrix into out[cols] (fp64
-// accumulation, deterministic two-pass).  ws needs colsum_ws_bytes().
+// Tensor-core (tcgen05, 3xTF32) product C = A . B^T (+ bias):
+// A [M, K] row-major with row stride lda, B [N, K] row-major with stride ldb,
+// C [M, N] with stride ldc.  A and B must be 16-byte aligned and lda, ldb
+// multiples of 4 (TMA); tc_gemm_supported() checks that.
+struct TcGemmArgs {
+  const float* A; long lda;
+  const float* B; long ldb;
+  float* C; long ldc;
+  const float* bias;
+  int M, N, K;
+};
+bool tc_gemm_supported(const TcGemmArgs& a);
+int tc_gemm(const TcGemmArgs& a, cudaStream_t stream, int kind);
+int read_gemm_status(int reset, int* status);
+
+// Small layout kernels: copy a [rows, cols] matrix into a row stride `ldd`
+// (pad columns zeroed), and transpose [rows, cols] into [cols, ldd].
+int pad_rows(const float* src, long rows, int cols, float* dst, int ldd, cudaStream_t stream);
+int transpose(const float* src, int rows, int cols, float* dst, int ldd, cudaStream_t stream);
+
+// Column sums of a [rows, cols] matrix with row stride ld into out[cols]
+// (fp64 accumulation, deterministic two-pass).  ws needs colsum_ws_bytes().
 size_t colsum_ws_bytes(long rows, int cols);
-int colsum(const float* X, long rows, int cols, float* out, void* ws, cudaStream_t stream);
+int colsum(const float* X, long rows, int cols, long ld, float* out, void* ws, cudaStream_t stream);
 
 int sm_count(int device);
 
@@ -99,7 +119,8 @@ enum KernelKind {
   kKindBwdRecurrent = 2,
   kKindGradGemm = 3,    // dW_hh, dW_ih, dx contractions (+ split-K reduce)
   kKindColsum = 4,      // db_ih / db_hh
-  kKindCount = 5
+  kKindLayout = 5,      // padding / transpose copies feeding the tensor-core products
+  kKindCount = 6
 };
 
 class LaunchScope {

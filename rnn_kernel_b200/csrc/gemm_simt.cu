@@ -96,12 +96,12 @@ int splits_for(int M, int N, int K, int device) {
   return S;
 }
 
-__global__ void colsum_partial_kernel(const float* X, long rows, int cols, long rchunk, double* part) {
+__global__ void colsum_partial_kernel(const float* X, long rows, int cols, long ld, long rchunk, double* part) {
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
   if (col >= cols) return;
   const long r0 = blockIdx.y * rchunk, r1 = min(rows, r0 + rchunk);
   double s = 0.0;
-  for (long r = r0; r < r1; ++r) s += X[r * cols + col];
+  for (long r = r0; r < r1; ++r) s += X[r * ld + col];
   part[(long)blockIdx.y * cols + col] = s;
 }
 
@@ -115,7 +115,47 @@ __global__ void colsum_final_kernel(const double* part, int nchunks, int cols, f
 
 constexpr int kColChunks = 256;
 
+__global__ void pad_rows_kernel(const float* src, long rows, int cols, float* dst, int ldd) {
+  const long n = rows * ldd;
+  for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < n; e += (long)gridDim.x * blockDim.x) {
+    const long r = e / ldd;
+    const int c = (int)(e - r * ldd);
+    dst[e] = c < cols ? src[r * cols + c] : 0.0f;
+  }
+}
+
+__global__ void transpose_kernel(const float* src, int rows, int cols, float* dst, int ldd) {
+  __shared__ float tile[32][33];
+  const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int r = r0 + i, c = c0 + threadIdx.x;
+    tile[i][threadIdx.x] = (r < rows && c < cols) ? src[(long)r * cols + c] : 0.0f;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int c = c0 + i, r = r0 + threadIdx.x;  // dst[c][r]
+    if (c < cols && r < ldd) dst[(long)c * ldd + r] = r < rows ? tile[threadIdx.x][i] : 0.0f;
+  }
+}
+
 }  // namespace
+
+int pad_rows(const float* src, long rows, int cols, float* dst, int ldd, cudaStream_t stream) {
+  if (rows <= 0) return GRU_OK;
+  LaunchScope scope(kKindLayout, stream);
+  pad_rows_kernel<<<1184, 256, 0, stream>>>(src, rows, cols, dst, ldd);
+  GRU_CUDA_TRY(cudaGetLastError());
+  return GRU_OK;
+}
+
+int transpose(const float* src, int rows, int cols, float* dst, int ldd, cudaStream_t stream) {
+  if (rows <= 0 || cols <= 0) return GRU_OK;
+  LaunchScope scope(kKindLayout, stream);
+  dim3 grid(ceil_div(cols, 32), ceil_div(ldd, 32));
+  transpose_kernel<<<grid, dim3(32, 8), 0, stream>>>(src, rows, cols, dst, ldd);
+  GRU_CUDA_TRY(cudaGetLastError());
+  return GRU_OK;
+}
 
 size_t gemm_ws_bytes(int M, int N, int K, int device) {
   const int S = splits_for(M, N, K, device);
@@ -154,13 +194,13 @@ int gemm(const GemmArgs& a, void* ws, size_t ws_bytes, int device, cudaStream_t 
 
 size_t colsum_ws_bytes(long rows, int cols) { return sizeof(double) * (size_t)kColChunks * cols; }
 
-int colsum(const float* X, long rows, int cols, float* out, void* ws, cudaStream_t stream) {
+int colsum(const float* X, long rows, int cols, long ld, float* out, void* ws, cudaStream_t stream) {
   if (cols <= 0) return GRU_OK;
   const long rchunk = (rows + kColChunks - 1) / kColChunks;
   double* part = static_cast<double*>(ws);
   dim3 grid(ceil_div(cols, 128), kColChunks);
   LaunchScope scope(kKindColsum, stream, 2);
-  colsum_partial_kernel<<<grid, 128, 0, stream>>>(X, rows, cols, rchunk > 0 ? rchunk : 1, part);
+  colsum_partial_kernel<<<grid, 128, 0, stream>>>(X, rows, cols, ld, rchunk > 0 ? rchunk : 1, part);
   GRU_CUDA_TRY(cudaGetLastError());
   colsum_final_kernel<<<ceil_div(cols, 128), 128, 0, stream>>>(part, kColChunks, cols, out);
   GRU_CUDA_TRY(cudaGetLastError());

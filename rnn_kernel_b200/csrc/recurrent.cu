@@ -303,7 +303,8 @@ struct BwdArgs {
   const float* dhn;    // [B,H] or null
   const float* w_hh;   // [3H,H]
   const float* stash;  // [B,T,5H]
-  float* dGi;          // [B,T,3H]
+  float* dGi;          // [B,T,3H] with row stride ldgi
+  int ldgi;
   float* dGh;          // [B,T,3H]
   float* dh0;          // [B,H]
 };
@@ -436,7 +437,7 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
         dgs[(s * 3 + 2) * 32 + jl] = dhn_gate;
         gz[b * Hc + jl] = gg * z;
         const size_t row = (size_t)(b_begin + b) * T + t;
-        float* gi = a.dGi + row * 3 * H + j;
+        float* gi = a.dGi + row * a.ldgi + j;
         float* gh = a.dGh + row * 3 * H + j;
         gi[0] = dr_pre;
         gi[H] = dz_pre;
@@ -661,9 +662,9 @@ int launch_rec_forward(const float* G, const float* h0, const float* w_hh, const
 }
 
 int launch_rec_backward(const float* dout, const float* dhn, const float* w_hh,
-                        const float* stash, float* dGi, float* dGh, float* dh0,
+                        const float* stash, float* dGi, int ldgi, float* dGh, float* dh0,
                         const RecGeom& g, cudaStream_t stream) {
-  BwdArgs a{dout, dhn, w_hh, stash, dGi, dGh, dh0};
+  BwdArgs a{dout, dhn, w_hh, stash, dGi, ldgi, dGh, dh0};
   return launch_clusters(kernel_for(false, g.R), a, g, stream, kKindBwdRecurrent);
 }
 
