@@ -77,6 +77,27 @@ int gru_backward(const float* dout, const float* dhn, const float* x, const floa
                  float* dw_hh, float* db_ih, float* db_hh, void* workspace,
                  size_t workspace_bytes, int B, int T, int I, int H, void* stream);
 
+/* Size of the static device scratch behind gru_forward_inference_noalloc. */
+#define GRU_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* Inference forward (no stash) that allocates nothing and takes no workspace.
+ * No counterpart in the reference.  For callers that cannot allocate device
+ * memory -- e.g. a plugin inside a host whose device memory is owned by the
+ * host's own allocator, or code running where an allocation would stall or
+ * is forbidden.  Same arguments and results as gru_forward(..., stash = NULL,
+ * ...) minus the workspace: the scratch is a fixed
+ * GRU_NOALLOC_SCRATCH_BYTES device array inside the library, held by every GPU
+ * that loads it until the process exits.  Shapes whose forward workspace
+ * (gru_forward_workspace_bytes) exceeds that size are rejected with
+ * GRU_ERR_UNSUPPORTED and a message.  The first call on a device looks up the
+ * array's device address (once per device, with that device current); make
+ * that first call before any stream capture.  All calls on a device share the
+ * one array, so calls that overlap on the GPU (different streams, no ordering
+ * between them) race; serialise them. */
+int gru_forward_inference_noalloc(const float* x, const float* h0, const float* w_ih,
+                                  const float* w_hh, const float* b_ih, const float* b_hh,
+                                  float* out, float* hn, int B, int T, int I, int H, void* stream);
+
 /* ---- Telemetry (no reference counterpart: the reference had no kernel
  * timers; its profiling scripts used torch.profiler / nsys, see
  * scripts/profile_a100_h256_step.py).  Kernel kinds: 0 input-projection GEMM,

@@ -28,6 +28,7 @@ SIGNATURES = {
     "gru_backward_workspace_bytes": (_size_t, [_int, _int, _int, _int]),
     "gru_forward": (_int, [_c_float_p] * 9 + [ctypes.c_void_p, _size_t] + [_int] * 4 + [ctypes.c_void_p]),
     "gru_backward": (_int, [_c_float_p] * 12 + [ctypes.c_void_p, _size_t] + [_int] * 4 + [ctypes.c_void_p]),
+    "gru_forward_inference_noalloc": (_int, [_c_float_p] * 8 + [_int] * 4 + [ctypes.c_void_p]),
     "gru_device_status": (_int, [_int]),
     "gru_launch_count": (ctypes.c_ulonglong, []),
     "gru_timing_enable": (_int, [_int]),
