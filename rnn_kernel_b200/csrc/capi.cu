@@ -88,6 +88,10 @@ FwdLayout fwd_layout(int B, int T, int I, int H) {
   return l;
 }
 
+// dW products run on the tensor cores when h_prev (stash stride 5H) and x
+// (stride I) have 16-byte row strides.
+inline bool dw_on_tensor_cores(int I, int H) { return H % 4 == 0 && I % 4 == 0; }
+
 struct BwdLayout {
   size_t dgi, dgh, wt, gemm, col, total;
   int ldgi;  // row stride of dG_ih (multiple of 4 floats for TMA)
@@ -101,12 +105,20 @@ BwdLayout bwd_layout(int B, int T, int I, int H, int device) {
   l.dgi = off;
   off = align_up(off + sizeof(float) * BT * l.ldgi, kAlign);
   l.dgh = off;
-  off = align_up(off + sizeof(float) * BT * 3 * H, kAlign);
+  off = align_up(off + sizeof(float) * BT * l.ldgi, kAlign);
   l.wt = off;
   off = align_up(off + sizeof(float) * (size_t)I * l.ldgi, kAlign);
   l.gemm = off;
-  size_t g = gemm_ws_bytes(3 * H, H, (int)BT, device);
-  g = std::max(g, gemm_ws_bytes(3 * H, I, (int)BT, device));
+  // Weight-gradient products: tensor cores (split-K partials) when the
+  // operands have 16-byte row strides, else the exact FP64 SIMT contraction.
+  size_t g = 0;
+  if (dw_on_tensor_cores(I, H)) {
+    TcGemmArgs hh{nullptr, l.ldgi, nullptr, 5L * H, nullptr, H, nullptr, 3 * H, H, (int)BT, true, true};
+    TcGemmArgs ih{nullptr, l.ldgi, nullptr, I, nullptr, I, nullptr, 3 * H, I, (int)BT, true, true};
+    g = std::max(tc_gemm_ws_bytes(hh, device), tc_gemm_ws_bytes(ih, device));
+  } else {
+    g = std::max(gemm_ws_bytes(3 * H, H, (int)BT, device), gemm_ws_bytes(3 * H, I, (int)BT, device));
+  }
   off = align_up(off + g, kAlign);
   l.col = off;
   off = align_up(off + colsum_ws_bytes(BT, 3 * H), kAlign);
@@ -273,12 +285,23 @@ int gru_backward(const float* dout, const float* dhn, const float* x, const floa
 
   const int BT = B * T;
   const int H3 = 3 * H;
-  // dW_hh = dG_hh^T . h_prev   (h_prev is stash column block 4)
-  GemmArgs a1{dGh, 1, H3, stash + 4 * H, 5L * H, 1, dw_hh, H, nullptr, H3, H, BT};
-  if ((rc = gemm(a1, gws, gws_bytes, dev, stream, kKindGradGemm, true))) return rc;
-  // dW_ih = dG_ih^T . x
-  GemmArgs a2{dGi, 1, l.ldgi, x, I, 1, dw_ih, I, nullptr, H3, I, BT};
-  if ((rc = gemm(a2, gws, gws_bytes, dev, stream, kKindGradGemm, true))) return rc;
+  // dW_hh = dG_hh^T . h_prev (h_prev = stash column block 4), dW_ih = dG_ih^T . x
+  if (dw_on_tensor_cores(I, H)) {
+    TcGemmArgs hh{dGh, l.ldgi, stash + 4 * H, 5L * H, dw_hh, H, nullptr, H3, H, BT, true, true};
+    TcGemmArgs ih{dGi, l.ldgi, x, I, dw_ih, I, nullptr, H3, I, BT, true, true};
+    if (tc_gemm_supported(hh) && tc_gemm_supported(ih)) {
+      if ((rc = tc_gemm(hh, stream, kKindGradGemm, gws, gws_bytes))) return rc;
+      if ((rc = tc_gemm(ih, stream, kKindGradGemm, gws, gws_bytes))) return rc;
+    } else {
+      set_error("gru_backward: x and stash must be 16-byte aligned");
+      return GRU_ERR_INVALID;
+    }
+  } else {
+    GemmArgs a1{dGh, 1, l.ldgi, stash + 4 * H, 5L * H, 1, dw_hh, H, nullptr, H3, H, BT};
+    if ((rc = gemm(a1, gws, gws_bytes, dev, stream, kKindGradGemm, true))) return rc;
+    GemmArgs a2{dGi, 1, l.ldgi, x, I, 1, dw_ih, I, nullptr, H3, I, BT};
+    if ((rc = gemm(a2, gws, gws_bytes, dev, stream, kKindGradGemm, true))) return rc;
+  }
   if (dx) {
     // dx = dG_ih . W_ih on the tensor cores, with W_ih^T staged as [I, ldgi].
     if ((rc = transpose(w_ih, H3, I, wt, l.ldgi, stream))) return rc;
@@ -286,7 +309,7 @@ int gru_backward(const float* dout, const float* dhn, const float* x, const floa
     if ((rc = tc_gemm(a3, stream, kKindGradGemm))) return rc;
   }
   if ((rc = colsum(dGi, BT, H3, l.ldgi, db_ih, ws + l.col, stream))) return rc;
-  if ((rc = colsum(dGh, BT, H3, H3, db_hh, ws + l.col, stream))) return rc;
+  if ((rc = colsum(dGh, BT, H3, l.ldgi, db_hh, ws + l.col, stream))) return rc;
   return GRU_OK;
 }
 

@@ -80,19 +80,24 @@ size_t gemm_ws_bytes(int M, int N, int K, int device);
 int gemm(const GemmArgs& a, void* ws, size_t ws_bytes, int device, cudaStream_t stream, int kind,
          bool exact = false);
 
-// Tensor-core (tcgen05, 3xTF32) product C = A . B^T (+ bias):
-// A [M, K] row-major with row stride lda, B [N, K] row-major with stride ldb,
-// C [M, N] with stride ldc.  A and B must be 16-byte aligned and lda, ldb
-// multiples of 4 (TMA); tc_gemm_supported() checks that.
+// Tensor-core (tcgen05, 3xTF32) product C[m, n] = sum_k A(m, k) B(n, k) (+ bias).
+// K-major operand (a_mn = false): A [M, K] row-major, row stride lda.
+// MN-major operand (a_mn = true): A stored [K, M] row-major (K is the row),
+// row stride lda; same for B with N.  C [M, N], row stride ldc.  Operands
+// must be 16-byte aligned and lda, ldb multiples of 4 floats (TMA);
+// tc_gemm_supported() checks that.  With ws != null and a long K the product
+// is split over K (partials in ws, FP64 reduce; bias must then be null).
 struct TcGemmArgs {
   const float* A; long lda;
   const float* B; long ldb;
   float* C; long ldc;
   const float* bias;
   int M, N, K;
+  bool a_mn = false, b_mn = false;
 };
 bool tc_gemm_supported(const TcGemmArgs& a);
-int tc_gemm(const TcGemmArgs& a, cudaStream_t stream, int kind);
+size_t tc_gemm_ws_bytes(const TcGemmArgs& a, int device);
+int tc_gemm(const TcGemmArgs& a, cudaStream_t stream, int kind, void* ws = nullptr, size_t ws_bytes = 0);
 int read_gemm_status(int reset, int* status);
 
 // Small layout kernels: copy a [rows, cols] matrix into a row stride `ldd`

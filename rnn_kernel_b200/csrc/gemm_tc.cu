@@ -106,9 +106,27 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   return d;
 }
 
-// Instruction descriptor: kind::tf32, D = F32, A = B = TF32, both K-major.
-__host__ __device__ constexpr uint32_t tf32_idesc(int M, int N) {
-  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+// Descriptor of an MN-major tf32 tile.  MN-major 32-bit operands use the
+// "128-byte swizzle, 32-byte atom" layout: 32-element (128-byte) wide column
+// blocks; within a block K rows of 128 bytes, swizzled in 32-byte granules
+// with a 4-row period (4-row atoms of 512 bytes = stride byte offset); blocks
+// along M/N are 4096 bytes apart (leading byte offset; one 32 x 32 TMA box
+// each, written with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B).
+__device__ __forceinline__ uint64_t sw128b32_desc_mn(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)(4096 >> 4) << 16;               // leading byte offset: next 32-wide M/N block
+  d |= (uint64_t)(512 >> 4) << 32;                // stride byte offset: next 4 K rows
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)1 << 61;                         // SWIZZLE_128B_BASE32B
+  return d;
+}
+
+// Instruction descriptor: kind::tf32, D = F32, A = B = TF32; bit 15/16 select
+// MN-major A/B.
+__host__ __device__ constexpr uint32_t tf32_idesc(int M, int N, bool a_mn, bool b_mn) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
@@ -132,34 +150,49 @@ struct Smem {
   static constexpr int kBytes = kBarOff + 256 + 1024;  // + barriers + alignment slack
 };
 
-// NACC tensor-memory accumulators of BN columns each: with NACC = 4 the
-// hi*hi products and the two cross products go to separate accumulators,
-// alternating between two of each by K stage, and the epilogue adds them in
-// FP32 (the tensor cores' own accumulation is less precise than an FP32
-// add, so fewer additions into any one accumulator keep the sum closer to
-// FP32 accuracy).
-template <int BN, int S, int NACC>
+// Accumulation.  The tensor cores' FP32 accumulation truncates instead of
+// rounding, which biases long sums toward zero (measured: -1.5e-7 relative
+// on K = 256 with one accumulator; ~1e-6 after 32 stages).  So every K stage
+// goes into a FRESH pair of tensor-memory accumulators (hi*hi products in one,
+// the two cross products in the other), NPAIR pairs in rotation, and the
+// epilogue warps drain each finished pair into FP32 registers with ordinary
+// round-to-nearest adds while the tensor cores work on the next stages.
+//
+// A_MN / B_MN: the operand is stored MN-major (its K index is the row), as for
+// the weight gradients dW = dG^T . X whose K is B*T.  Split-K: blockIdx.y
+// selects a K range of `kchunk` elements and, with gridDim.y > 1, the tile is
+// written to C + blockIdx.y * M * ldc (a partial, no bias) for a later reduce.
+template <int BN, int S, int NPAIR, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                   float* __restrict__ C, long ldc, const float* __restrict__ bias, int M, int N, int K) {
+                   float* __restrict__ C, long ldc, const float* __restrict__ bias, int M, int N, int K,
+                   int kchunk) {
   using L = Smem<BN, S>;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled tiles.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bars = sbase + L::kBarOff;
-  // barriers: full[S], ready[S], empty[S], accum; then the TMEM address slot
+  // barriers: full[S], ready[S], empty[S], filled[NPAIR], drained[NPAIR]; then the TMEM slot
   auto full = [&](int s) { return bars + 8u * s; };
   auto ready = [&](int s) { return bars + 8u * (S + s); };
   auto empty = [&](int s) { return bars + 8u * (2 * S + s); };
-  const uint32_t accum = bars + 8u * (3 * S);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kBarOff + 8 * (3 * S + 1));
+  auto filled = [&](int p) { return bars + 8u * (3 * S + p); };
+  auto drained = [&](int p) { return bars + 8u * (3 * S + NPAIR + p); };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kBarOff + 8 * (3 * S + 2 * NPAIR));
+  constexpr int kCols = 2 * NPAIR * BN;  // tensor-memory columns allocated
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_n = (N + BN - 1) / BN;
   const int m0 = (blockIdx.x / tiles_n) * kBM;
   const int n0 = (blockIdx.x % tiles_n) * BN;
-  const int nk = (K + kBK - 1) / kBK;
+  const int kbeg = blockIdx.y * kchunk;
+  const int kend = min(K, kbeg + kchunk);
+  const int nk = kend > kbeg ? (kend - kbeg + kBK - 1) / kBK : 0;
+  if (gridDim.y > 1) {
+    C += (long)blockIdx.y * M * ldc;
+    bias = nullptr;
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -167,12 +200,15 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
       mbar_init(ready(s), kTransformThreads);
       mbar_init(empty(s), 1);
     }
-    mbar_init(accum, 1);
+    for (int p = 0; p < NPAIR; ++p) {
+      mbar_init(filled(p), 1);
+      mbar_init(drained(p), 128);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(BN * NACC)
+                 "r"(kCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -188,94 +224,123 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
         if (i >= S && !mbar_wait(empty(s), ((i / S) - 1) & 1)) break;
         const uint32_t st = sbase + s * L::kStage;
         mbar_arrive_expect_tx(full(s), L::kATile + L::kBTile);
-        tma_load_2d(st, &map_a, full(s), i * kBK, m0);
-        tma_load_2d(st + 2 * L::kATile, &map_b, full(s), i * kBK, n0);
+        const int k0 = kbeg + i * kBK;
+        if (A_MN) {
+#pragma unroll
+          for (int j = 0; j < kBM / 32; ++j) tma_load_2d(st + j * 4096, &map_a, full(s), m0 + 32 * j, k0);
+        } else {
+          tma_load_2d(st, &map_a, full(s), k0, m0);
+        }
+        if (B_MN) {
+#pragma unroll
+          for (int j = 0; j < BN / 32; ++j)
+            tma_load_2d(st + 2 * L::kATile + j * 4096, &map_b, full(s), n0 + 32 * j, k0);
+        } else {
+          tma_load_2d(st + 2 * L::kATile, &map_b, full(s), k0, n0);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = tf32_idesc(kBM, BN);
+      const uint32_t idesc = tf32_idesc(kBM, BN, A_MN, B_MN);
+      // 8-wide K steps: 32 bytes along a K-major row, or 8 rows (1024 bytes)
+      // of an MN-major block.
+      auto da = [&](uint32_t base, int kk) {
+        return A_MN ? sw128b32_desc_mn(base + kk * 1024) : sw128_desc(base + kk * 32);
+      };
+      auto db = [&](uint32_t base, int kk) {
+        return B_MN ? sw128b32_desc_mn(base + kk * 1024) : sw128_desc(base + kk * 32);
+      };
       for (int i = 0; i < nk; ++i) {
-        const int s = i % S;
+        const int s = i % S, p = i % NPAIR;
         if (!mbar_wait(ready(s), (i / S) & 1)) break;
+        if (i >= NPAIR && !mbar_wait(drained(p), ((i / NPAIR) - 1) & 1)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t st = sbase + s * L::kStage;
         const uint32_t a_hi = st, a_lo = st + L::kATile, b_hi = st + 2 * L::kATile, b_lo = b_hi + L::kBTile;
-        // Accumulators: [0, NACC/2) hold hi*hi, [NACC/2, NACC) the cross terms.
-        const int half = NACC / 2;
-        const uint32_t d_big = tmem + (uint32_t)(BN * (i % half));
-        const uint32_t d_small = tmem + (uint32_t)(BN * (half + i % half));
-        const uint32_t fresh = (i < half) ? 1u : 0u;
+        const uint32_t d_big = tmem + (uint32_t)(BN * (2 * p));
+        const uint32_t d_small = tmem + (uint32_t)(BN * (2 * p + 1));
 #pragma unroll
         for (int kk = 0; kk < kBK / 8; ++kk) {
-          const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along the swizzled row
-          const uint32_t acc = (fresh && kk == 0) ? 0u : 1u;
-          mma_tf32(d_small, sw128_desc(a_lo + off), sw128_desc(b_hi + off), idesc, acc);
-          mma_tf32(d_small, sw128_desc(a_hi + off), sw128_desc(b_lo + off), idesc, 1u);
-          mma_tf32(d_big, sw128_desc(a_hi + off), sw128_desc(b_hi + off), idesc, acc);
+          const uint32_t acc = kk == 0 ? 0u : 1u;
+          mma_tf32(d_small, da(a_lo, kk), db(b_hi, kk), idesc, acc);
+          mma_tf32(d_small, da(a_hi, kk), db(b_lo, kk), idesc, 1u);
+          mma_tf32(d_big, da(a_hi, kk), db(b_hi, kk), idesc, acc);
         }
         mma_commit(empty(s));
+        mma_commit(filled(p));
       }
-      mma_commit(accum);
     }
   } else {
-    // Transform warps 2..7: split each landed stage into hi (in place) + lo.
+    // Warps 2..7 split each landed stage into hi (in place) + lo; warps 4..7
+    // also drain the accumulator pair of the previous stage into registers.
     const int tt = threadIdx.x - 64;
     constexpr int kA4 = L::kATile / 16, kB4 = L::kBTile / 16;  // float4 count per tile
-    for (int i = 0; i < nk; ++i) {
-      const int s = i % S;
-      if (!mbar_wait(full(s), (i / S) & 1)) break;
-      float4* a = reinterpret_cast<float4*>(smem + s * L::kStage);
-      float4* alo = a + kA4;
-      float4* b = alo + kA4;
-      float4* blo = b + kB4;
-      for (int e = tt; e < kA4 + kB4; e += kTransformThreads) {
-        float4* src = e < kA4 ? a + e : b + (e - kA4);
-        float4* dlo = e < kA4 ? alo + e : blo + (e - kA4);
-        const float4 v = *src;
-        uint4 hi, lo;
-        hi.x = to_tf32(v.x); hi.y = to_tf32(v.y); hi.z = to_tf32(v.z); hi.w = to_tf32(v.w);
-        lo.x = to_tf32(v.x - __uint_as_float(hi.x));
-        lo.y = to_tf32(v.y - __uint_as_float(hi.y));
-        lo.z = to_tf32(v.z - __uint_as_float(hi.z));
-        lo.w = to_tf32(v.w - __uint_as_float(hi.w));
-        *reinterpret_cast<uint4*>(src) = hi;
-        *reinterpret_cast<uint4*>(dlo) = lo;
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      mbar_arrive(ready(s));
-    }
-    if (warp >= 4) {
-      // Epilogue: this warp owns accumulator lanes 32*(warp%4) .. +32.
-      const bool ok = mbar_wait(accum, 0);
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int row = m0 + 32 * (warp & 3) + lane;
-      const uint32_t taddr = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
-      const int used = nk < NACC / 2 ? nk : NACC / 2;  // accumulator pairs written
-      for (int c0 = 0; c0 < BN && ok; c0 += 16) {
-        float v[16];
+    const bool drainer = warp >= 4;
+    const uint32_t taddr = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+    float acc[BN];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = 0.0f;
-        // cross terms first (small), then the hi*hi sums
-        for (int q = NACC - 1; q >= 0; --q) {
-          if ((q % (NACC / 2)) >= used) continue;
-          uint32_t r[16];
+    for (int c = 0; c < BN; ++c) acc[c] = 0.0f;
+    bool ok = true;
+    for (int i = 0; i <= nk && ok; ++i) {
+      if (i < nk) {
+        const int s = i % S;
+        if (!mbar_wait(full(s), (i / S) & 1)) { ok = false; break; }
+        float4* a = reinterpret_cast<float4*>(smem + s * L::kStage);
+        float4* alo = a + kA4;
+        float4* b = alo + kA4;
+        float4* blo = b + kB4;
+        for (int e = tt; e < kA4 + kB4; e += kTransformThreads) {
+          float4* src = e < kA4 ? a + e : b + (e - kA4);
+          float4* dlo = e < kA4 ? alo + e : blo + (e - kA4);
+          const float4 v = *src;
+          uint4 hi, lo;
+          hi.x = to_tf32(v.x); hi.y = to_tf32(v.y); hi.z = to_tf32(v.z); hi.w = to_tf32(v.w);
+          lo.x = to_tf32(v.x - __uint_as_float(hi.x));
+          lo.y = to_tf32(v.y - __uint_as_float(hi.y));
+          lo.z = to_tf32(v.z - __uint_as_float(hi.z));
+          lo.w = to_tf32(v.w - __uint_as_float(hi.w));
+          *reinterpret_cast<uint4*>(src) = hi;
+          *reinterpret_cast<uint4*>(dlo) = lo;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive(ready(s));
+      }
+      if (drainer && i >= 1) {
+        const int d = i - 1, p = d % NPAIR;
+        if (!mbar_wait(filled(p), (d / NPAIR) & 1)) { ok = false; break; }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          uint32_t rs[16], rb[16];
           asm volatile(
               "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-              : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-                "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-              : "r"(taddr + (uint32_t)(q * BN + c0)));
+              : "=r"(rs[0]), "=r"(rs[1]), "=r"(rs[2]), "=r"(rs[3]), "=r"(rs[4]), "=r"(rs[5]), "=r"(rs[6]),
+                "=r"(rs[7]), "=r"(rs[8]), "=r"(rs[9]), "=r"(rs[10]), "=r"(rs[11]), "=r"(rs[12]), "=r"(rs[13]),
+                "=r"(rs[14]), "=r"(rs[15])
+              : "r"(taddr + (uint32_t)(BN * (2 * p + 1) + c0)));
+          asm volatile(
+              "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+              : "=r"(rb[0]), "=r"(rb[1]), "=r"(rb[2]), "=r"(rb[3]), "=r"(rb[4]), "=r"(rb[5]), "=r"(rb[6]),
+                "=r"(rb[7]), "=r"(rb[8]), "=r"(rb[9]), "=r"(rb[10]), "=r"(rb[11]), "=r"(rb[12]), "=r"(rb[13]),
+                "=r"(rb[14]), "=r"(rb[15])
+              : "r"(taddr + (uint32_t)(BN * (2 * p) + c0)));
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] += __uint_as_float(r[j]);
+          for (int jj = 0; jj < 16; ++jj) acc[c0 + jj] += __uint_as_float(rb[jj]) + __uint_as_float(rs[jj]);
         }
-        if (row < M) {
-          float* crow = C + (long)row * ldc;
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        mbar_arrive(drained(p));
+      }
+    }
+    if (drainer && ok) {
+      const int row = m0 + 32 * (warp & 3) + lane;
+      if (row < M) {
+        float* crow = C + (long)row * ldc;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int n = n0 + c0 + j;
-            if (n < N) crow[n] = v[j] + (bias ? bias[n] : 0.0f);
-          }
+        for (int c = 0; c < BN; ++c) {
+          const int n = n0 + c;
+          if (n < N) crow[n] = acc[c] + (bias ? bias[n] : 0.0f);
         }
       }
     }
@@ -284,10 +349,9 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
   __syncthreads();
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN * NACC) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
   }
 }
-
 
 // cuTensorMapEncodeTiled reached through the runtime's driver entry point, so
 // the library does not link libcuda directly (it still loads on machines
@@ -312,21 +376,64 @@ int encode_fn(EncodeTiledFn* out) {
   return GRU_OK;
 }
 
-int make_map(CUtensorMap* map, const float* ptr, int rows, int k, long ld, int box_rows) {
+// 2-D fp32 tensor map over a row-major [rows, cols] matrix (row stride ld
+// floats), box = box_cols (inner) x box_rows, 128-byte swizzle.
+int make_map(CUtensorMap* map, const float* ptr, long rows, long cols, long ld, int box_cols, int box_rows,
+             bool mn_major) {
   EncodeTiledFn enc = nullptr;
   int rc = encode_fn(&enc);
   if (rc) return rc;
-  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
-  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed with CUresult " + std::to_string((int)r));
     return GRU_ERR_CUDA;
   }
+  return GRU_OK;
+}
+
+__global__ void splitk_sum_kernel(const float* __restrict__ part, int S, int M, int N, long ldp,
+                                  float* __restrict__ C, long ldc) {
+  const long MN = (long)M * N;
+  for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < MN; e += (long)gridDim.x * blockDim.x) {
+    const int m = (int)(e / N), n = (int)(e - (long)m * N);
+    double acc = 0.0;
+    for (int z = 0; z < S; ++z) acc += part[((long)z * M + m) * ldp + n];
+    C[(long)m * ldc + n] = (float)acc;
+  }
+}
+
+constexpr int kBN = 64, kS = 4, kNPAIR = 4;
+using LDefault = Smem<kBN, kS>;
+
+template <bool A_MN, bool B_MN>
+int launch_tc(const TcGemmArgs& a, float* C, long ldc, const float* bias, int splits, int kchunk,
+              cudaStream_t stream) {
+  auto kern = gemm_tf32x3_kernel<kBN, kS, kNPAIR, A_MN, B_MN>;
+  static thread_local int configured_device = -1;
+  int dev = 0;
+  GRU_CUDA_TRY(cudaGetDevice(&dev));
+  if (configured_device != dev) {
+    GRU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, LDefault::kBytes));
+    configured_device = dev;
+  }
+  CUtensorMap ma, mb;
+  int rc = A_MN ? make_map(&ma, a.A, a.K, a.M, a.lda, 32, kBK, true)
+                : make_map(&ma, a.A, a.M, a.K, a.lda, kBK, kBM, false);
+  if (rc) return rc;
+  rc = B_MN ? make_map(&mb, a.B, a.K, a.N, a.ldb, 32, kBK, true)
+            : make_map(&mb, a.B, a.N, a.K, a.ldb, kBK, kBN, false);
+  if (rc) return rc;
+  dim3 grid(((a.M + kBM - 1) / kBM) * ((a.N + kBN - 1) / kBN), splits);
+  kern<<<grid, kThreads, LDefault::kBytes, stream>>>(ma, mb, C, ldc, bias, a.M, a.N, a.K, kchunk);
+  GRU_CUDA_TRY(cudaGetLastError());
   return GRU_OK;
 }
 
@@ -342,34 +449,62 @@ int read_gemm_status(int reset, int* status) {
 }
 
 bool tc_gemm_supported(const TcGemmArgs& a) {
-  return ((reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.B)) & 15) == 0 && a.lda % 4 == 0 &&
-         a.ldb % 4 == 0 && a.K >= 1;
+  return ((reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.B)) & 15) == 0 &&
+         a.lda % 4 == 0 && a.ldb % 4 == 0 && a.K >= 1;
 }
 
-int tc_gemm(const TcGemmArgs& a, cudaStream_t stream, int kind) {
+int tc_splits(const TcGemmArgs& a, int device) {
+  // Long K (the weight gradients, K = B*T) with few output tiles: split K so
+  // the grid covers the SMs about twice, keeping >= 8 K stages per split.
+  const int tiles = ((a.M + kBM - 1) / kBM) * ((a.N + kBN - 1) / kBN);
+  const int stages = (a.K + kBK - 1) / kBK;
+  int s = (2 * sm_count(device) + tiles - 1) / tiles;
+  if (s > stages / 8) s = stages / 8;
+  return s < 1 ? 1 : s;
+}
+
+size_t tc_gemm_ws_bytes(const TcGemmArgs& a, int device) {
+  const int s = tc_splits(a, device);
+  return s > 1 ? sizeof(float) * (size_t)s * a.M * a.N : 0;
+}
+
+int tc_gemm(const TcGemmArgs& a, cudaStream_t stream, int kind, void* ws, size_t ws_bytes) {
   if (a.M <= 0 || a.N <= 0) return GRU_OK;
   if (!tc_gemm_supported(a)) {
     set_error("tc_gemm: operands must be 16-byte aligned with row strides a multiple of 4 floats");
     return GRU_ERR_INVALID;
   }
-  constexpr int BN = 64, S = 4, NACC = 8;
-  using L = Smem<BN, S>;
-  static thread_local int configured_device = -1;
   int dev = 0;
   GRU_CUDA_TRY(cudaGetDevice(&dev));
-  if (configured_device != dev) {
-    GRU_CUDA_TRY(cudaFuncSetAttribute(gemm_tf32x3_kernel<BN, S, NACC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      L::kBytes));
-    configured_device = dev;
+  const int splits = ws ? tc_splits(a, dev) : 1;
+  const int kchunk = splits > 1 ? ((a.K + splits * kBK - 1) / (splits * kBK)) * kBK : a.K;
+  float* C = a.C;
+  long ldc = a.ldc;
+  if (splits > 1) {
+    if (ws_bytes < tc_gemm_ws_bytes(a, dev)) {
+      set_error("tc_gemm: split-K workspace too small");
+      return GRU_ERR_INVALID;
+    }
+    C = static_cast<float*>(ws);
+    ldc = a.N;
   }
-  CUtensorMap ma, mb;
-  int rc = make_map(&ma, a.A, a.M, a.K, a.lda, kBM);
+  LaunchScope scope(kind, stream, splits > 1 ? 2 : 1);
+  int rc;
+  if (a.a_mn && a.b_mn) rc = launch_tc<true, true>(a, C, ldc, a.bias, splits, kchunk, stream);
+  else if (!a.a_mn && !a.b_mn) rc = launch_tc<false, false>(a, C, ldc, a.bias, splits, kchunk, stream);
+  else {
+    set_error("tc_gemm: mixed operand majors are not instantiated");
+    return GRU_ERR_INVALID;
+  }
   if (rc) return rc;
-  if ((rc = make_map(&mb, a.B, a.N, a.K, a.ldb, BN))) return rc;
-  const int tiles = ((a.M + kBM - 1) / kBM) * ((a.N + BN - 1) / BN);
-  LaunchScope scope(kind, stream);
-  gemm_tf32x3_kernel<BN, S, NACC><<<tiles, kThreads, L::kBytes, stream>>>(ma, mb, a.C, a.ldc, a.bias, a.M, a.N, a.K);
-  GRU_CUDA_TRY(cudaGetLastError());
+  if (splits > 1) {
+    if (a.bias) {
+      set_error("tc_gemm: bias with split-K is not supported");
+      return GRU_ERR_INVALID;
+    }
+    splitk_sum_kernel<<<sm_count(dev) * 4, 256, 0, stream>>>(C, splits, a.M, a.N, a.N, a.C, a.ldc);
+    GRU_CUDA_TRY(cudaGetLastError());
+  }
   return GRU_OK;
 }
 

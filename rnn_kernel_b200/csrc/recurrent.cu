@@ -305,7 +305,7 @@ struct BwdArgs {
   const float* stash;  // [B,T,5H]
   float* dGi;          // [B,T,3H] with row stride ldgi
   int ldgi;
-  float* dGh;          // [B,T,3H]
+  float* dGh;          // [B,T,3H] with row stride ldgi
   float* dh0;          // [B,H]
 };
 
@@ -438,7 +438,7 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
         gz[b * Hc + jl] = gg * z;
         const size_t row = (size_t)(b_begin + b) * T + t;
         float* gi = a.dGi + row * a.ldgi + j;
-        float* gh = a.dGh + row * 3 * H + j;
+        float* gh = a.dGh + row * a.ldgi + j;
         gi[0] = dr_pre;
         gi[H] = dz_pre;
         gi[2 * H] = dn_pre;

@@ -19,11 +19,12 @@ itself misses that element-wise bar by up to 8x at BASELINE config 2.  For
 those tensors ``weights="envelope"`` requires the max error against the truth
 to stay within 3x of torch FP32's own (plus atol) and the normwise relative
 error ||ours - truth||_F / ||truth||_F to stay below 1e-6.  The factor
-is not 1 because the input projection runs on the tensor cores: their FP32
-accumulation truncates, a measured relative bias of -1.5e-7 on G = x.W_ih^T
-(FP32 FMA: ~0), which adds up coherently in dW_ih = sum dG_ih * x over
-B*T = 131k terms: 2.3x torch's max error and 4x its RMS error there, i.e.
-3.5e-7 of the largest entry and ~4e-7 normwise.
+is not 1 because
+the input projection and dx run on the tensor cores, whose FP32 accumulation
+truncates.  The GEMM drains a fresh accumulator per 32-wide K stage into FP32
+registers, which leaves a measured relative shrink bias of -8.6e-8 on
+G = x.W_ih^T (FP32 FMA: ~0); summed coherently in dW_ih = sum dG_ih * x over
+B*T = 131k terms (config 4) that stays inside the envelope.
 Every other tensor stays strict.
 """
 from __future__ import annotations
