@@ -49,7 +49,8 @@ struct RecGeom {
   size_t smem;  // dynamic shared memory bytes per CTA
 };
 
-constexpr int kMaxRows = 8;  // largest GEMV sub-chunk (batch rows)
+constexpr int kMaxRows = 8;     // largest GEMV sub-chunk (batch rows)
+constexpr int kMaxCluster = 8;  // CTAs per cluster for H <= 256
 
 int read_device_status(int reset, int* status);
 int rec_forward_geometry(int B, int T, int H, int device, RecGeom* g);

@@ -155,6 +155,7 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
   float* hbuf = smem;                          // [2][bcp][Kp]
   float* part = smem + g.off1;                 // [nw][R][3][32]
   float* ring = smem + g.off2;                 // [pd][bcp][3][Hc]
+  float* bsl = smem + g.off3;                  // [3][Hc] this CTA's slice of b_hh
   const int ring_stride = bcp * 3 * Hc;
   const int slot_stride = bcp * Kp;
 
@@ -178,6 +179,10 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
 
   for (int e = tid; e < 2 * slot_stride; e += nthr) hbuf[e] = 0.0f;
   for (int e = tid; e < g.nw * R * 3 * 32; e += nthr) part[e] = 0.0f;
+  for (int e = tid; e < 3 * Hc; e += nthr) {
+    const int q = e / Hc, jl = e - q * Hc;
+    bsl[e] = jl < hcnt ? a.b_hh[q * H + j0 + jl] : 0.0f;
+  }
   __syncthreads();
   for (int e = tid; e < nb * H; e += nthr) {
     const int b = e / H, k = e - b * H;
@@ -258,16 +263,22 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
       for (int e = tid; e < ns * hcnt; e += nthr) {
         const int s = e / hcnt, jl = e - s * hcnt;
         const int b = b0 + s, j = j0 + jl;
-        float ar = 0.0f, az = 0.0f, an = 0.0f;
-        for (int w = 0; w < g.nw; ++w) {
+        float ar = bsl[jl], az = bsl[Hc + jl], an = bsl[2 * Hc + jl];
+        float pr[kMaxCluster], pz[kMaxCluster], pn[kMaxCluster];
+#pragma unroll
+        for (int w = 0; w < kMaxCluster; ++w) {
           const float* p = part + ((w * R + s) * 3) * 32 + jl;
-          ar += p[0];
-          az += p[32];
-          an += p[64];
+          const bool v = w < g.nw;
+          pr[w] = v ? p[0] : 0.0f;
+          pz[w] = v ? p[32] : 0.0f;
+          pn[w] = v ? p[64] : 0.0f;
         }
-        ar += a.b_hh[j];
-        az += a.b_hh[H + j];
-        an += a.b_hh[2 * H + j];
+#pragma unroll
+        for (int w = 0; w < kMaxCluster; ++w) {
+          ar += pr[w];
+          az += pz[w];
+          an += pn[w];
+        }
         const float* gi = rg + (b * 3) * Hc + jl;
         const float r = sigmoidf_acc(gi[0] + ar);
         const float z = sigmoidf_acc(gi[Hc] + az);
@@ -419,8 +430,12 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
         if (it == 0) {
           dh = (a.dhn != nullptr) ? a.dhn[(size_t)(b_begin + b) * H + j] : 0.0f;
         } else {
+          float pp[kMaxCluster];
+#pragma unroll
+          for (int q = 0; q < kMaxCluster; ++q) pp[q] = q < C ? rin[(q * bcp + b) * Hc + jl] : 0.0f;
           dh = gz[b * Hc + jl];
-          for (int q = 0; q < C; ++q) dh += rin[(q * bcp + b) * Hc + jl];
+#pragma unroll
+          for (int q = 0; q < kMaxCluster; ++q) dh += pp[q];
         }
         const float* v = rg + (b * 6) * Hc + jl;
         const float gg = dh + v[0];
@@ -523,7 +538,7 @@ size_t fwd_smem(RecGeom& g) {
   g.off1 = round4((size_t)2 * g.bcp * Kp);
   g.off2 = g.off1 + round4((size_t)g.nw * g.R * 3 * 32);
   g.off3 = g.off2 + round4((size_t)g.pd * g.bcp * 3 * g.Hc);
-  return sizeof(float) * (size_t)g.off3;
+  return sizeof(float) * (size_t)(g.off3 + round4((size_t)3 * g.Hc));
 }
 size_t bwd_smem(RecGeom& g) {
   g.off1 = round4((size_t)2 * g.C * g.bcp * g.Hc);
