@@ -159,14 +159,37 @@ struct Smem {
 // round-to-nearest adds while the tensor cores work on the next stages.
 //
 // A_MN / B_MN: the operand is stored MN-major (its K index is the row), as for
-// the weight gradients dW = dG^T . X whose K is B*T.  Split-K: blockIdx.y
-// selects a K range of `kchunk` elements and, with gridDim.y > 1, the tile is
-// written to C + blockIdx.y * M * ldc (a partial, no bias) for a later reduce.
+// the weight gradients dW = dG^T . X whose K is B*T.
+//
+// Persistent: the grid has at most one CTA per SM, and each CTA walks the
+// work units u = blockIdx.x, blockIdx.x + gridDim.x, ... where a unit is one
+// 128 x BN output tile of one K split (splits > 1 write FP32 partials to
+// C + split * M * ldc, without bias, for a later FP64 reduce).  The stage
+// ring, the accumulator pairs and their mbarrier phases continue across units,
+// so loads of the next tile overlap the drain and stores of the previous one.
+struct Unit {
+  int m0, n0, kbeg, nk, split;
+};
+
+template <int BN>
+__device__ __forceinline__ Unit unit_of(int u, int tiles_n, int tiles, int M, int K, int kchunk) {
+  Unit w;
+  const int tile = u % tiles;
+  w.split = u / tiles;
+  w.m0 = (tile / tiles_n) * kBM;
+  w.n0 = (tile % tiles_n) * BN;
+  w.kbeg = w.split * kchunk;
+  const int kend = min(K, w.kbeg + kchunk);
+  w.nk = kend > w.kbeg ? (kend - w.kbeg + kBK - 1) / kBK : 0;
+  (void)M;
+  return w;
+}
+
 template <int BN, int S, int NPAIR, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    float* __restrict__ C, long ldc, const float* __restrict__ bias, int M, int N, int K,
-                   int kchunk) {
+                   int kchunk, int splits) {
   using L = Smem<BN, S>;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled tiles.
@@ -184,15 +207,8 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_n = (N + BN - 1) / BN;
-  const int m0 = (blockIdx.x / tiles_n) * kBM;
-  const int n0 = (blockIdx.x % tiles_n) * BN;
-  const int kbeg = blockIdx.y * kchunk;
-  const int kend = min(K, kbeg + kchunk);
-  const int nk = kend > kbeg ? (kend - kbeg + kBK - 1) / kBK : 0;
-  if (gridDim.y > 1) {
-    C += (long)blockIdx.y * M * ldc;
-    bias = nullptr;
-  }
+  const int tiles = ((M + kBM - 1) / kBM) * tiles_n;
+  const int units = tiles * splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -205,6 +221,10 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
       mbar_init(drained(p), 128);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0 && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)) : "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -219,24 +239,29 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int i = 0; i < nk; ++i) {
-        const int s = i % S;
-        if (i >= S && !mbar_wait(empty(s), ((i / S) - 1) & 1)) break;
-        const uint32_t st = sbase + s * L::kStage;
-        mbar_arrive_expect_tx(full(s), L::kATile + L::kBTile);
-        const int k0 = kbeg + i * kBK;
-        if (A_MN) {
+      int i = 0;  // global stage counter of this CTA
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const Unit w = unit_of<BN>(u, tiles_n, tiles, M, K, kchunk);
+        for (int ks = 0; ks < w.nk; ++ks, ++i) {
+          const int s = i % S;
+          if (i >= S && !mbar_wait(empty(s), ((i / S) - 1) & 1)) { ok = false; break; }
+          const uint32_t st = sbase + s * L::kStage;
+          mbar_arrive_expect_tx(full(s), L::kATile + L::kBTile);
+          const int k0 = w.kbeg + ks * kBK;
+          if (A_MN) {
 #pragma unroll
-          for (int j = 0; j < kBM / 32; ++j) tma_load_2d(st + j * 4096, &map_a, full(s), m0 + 32 * j, k0);
-        } else {
-          tma_load_2d(st, &map_a, full(s), k0, m0);
-        }
-        if (B_MN) {
+            for (int j = 0; j < kBM / 32; ++j) tma_load_2d(st + j * 4096, &map_a, full(s), w.m0 + 32 * j, k0);
+          } else {
+            tma_load_2d(st, &map_a, full(s), k0, w.m0);
+          }
+          if (B_MN) {
 #pragma unroll
-          for (int j = 0; j < BN / 32; ++j)
-            tma_load_2d(st + 2 * L::kATile + j * 4096, &map_b, full(s), n0 + 32 * j, k0);
-        } else {
-          tma_load_2d(st + 2 * L::kATile, &map_b, full(s), k0, n0);
+            for (int j = 0; j < BN / 32; ++j)
+              tma_load_2d(st + 2 * L::kATile + j * 4096, &map_b, full(s), w.n0 + 32 * j, k0);
+          } else {
+            tma_load_2d(st + 2 * L::kATile, &map_b, full(s), k0, w.n0);
+          }
         }
       }
     }
@@ -251,29 +276,35 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
       auto db = [&](uint32_t base, int kk) {
         return B_MN ? sw128b32_desc_mn(base + kk * 1024) : sw128_desc(base + kk * 32);
       };
-      for (int i = 0; i < nk; ++i) {
-        const int s = i % S, p = i % NPAIR;
-        if (!mbar_wait(ready(s), (i / S) & 1)) break;
-        if (i >= NPAIR && !mbar_wait(drained(p), ((i / NPAIR) - 1) & 1)) break;
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t st = sbase + s * L::kStage;
-        const uint32_t a_hi = st, a_lo = st + L::kATile, b_hi = st + 2 * L::kATile, b_lo = b_hi + L::kBTile;
-        const uint32_t d_big = tmem + (uint32_t)(BN * (2 * p));
-        const uint32_t d_small = tmem + (uint32_t)(BN * (2 * p + 1));
+      int i = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const Unit w = unit_of<BN>(u, tiles_n, tiles, M, K, kchunk);
+        for (int ks = 0; ks < w.nk; ++ks, ++i) {
+          const int s = i % S, p = i % NPAIR;
+          if (!mbar_wait(ready(s), (i / S) & 1)) { ok = false; break; }
+          if (i >= NPAIR && !mbar_wait(drained(p), ((i / NPAIR) - 1) & 1)) { ok = false; break; }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t st = sbase + s * L::kStage;
+          const uint32_t a_hi = st, a_lo = st + L::kATile, b_hi = st + 2 * L::kATile, b_lo = b_hi + L::kBTile;
+          const uint32_t d_big = tmem + (uint32_t)(BN * (2 * p));
+          const uint32_t d_small = tmem + (uint32_t)(BN * (2 * p + 1));
 #pragma unroll
-        for (int kk = 0; kk < kBK / 8; ++kk) {
-          const uint32_t acc = kk == 0 ? 0u : 1u;
-          mma_tf32(d_small, da(a_lo, kk), db(b_hi, kk), idesc, acc);
-          mma_tf32(d_small, da(a_hi, kk), db(b_lo, kk), idesc, 1u);
-          mma_tf32(d_big, da(a_hi, kk), db(b_hi, kk), idesc, acc);
+          for (int kk = 0; kk < kBK / 8; ++kk) {
+            const uint32_t acc = kk == 0 ? 0u : 1u;
+            mma_tf32(d_small, da(a_lo, kk), db(b_hi, kk), idesc, acc);
+            mma_tf32(d_small, da(a_hi, kk), db(b_lo, kk), idesc, 1u);
+            mma_tf32(d_big, da(a_hi, kk), db(b_hi, kk), idesc, acc);
+          }
+          mma_commit(empty(s));
+          mma_commit(filled(p));
         }
-        mma_commit(empty(s));
-        mma_commit(filled(p));
       }
     }
   } else {
     // Warps 2..7 split each landed stage into hi (in place) + lo; warps 4..7
-    // also drain the accumulator pair of the previous stage into registers.
+    // also drain the accumulator pair of the previous stage into registers
+    // and store each finished tile.
     const int tt = threadIdx.x - 64;
     constexpr int kA4 = L::kATile / 16, kB4 = L::kBTile / 16;  // float4 count per tile
     const bool drainer = warp >= 4;
@@ -282,8 +313,78 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
 #pragma unroll
     for (int c = 0; c < BN; ++c) acc[c] = 0.0f;
     bool ok = true;
-    for (int i = 0; i <= nk && ok; ++i) {
-      if (i < nk) {
+    int i = 0;       // stage being transformed
+    int d = 0;       // stage being drained
+    int du = blockIdx.x, dks = 0;  // unit and in-unit stage of stage d
+    Unit dw = unit_of<BN>(du, tiles_n, tiles, M, K, kchunk);
+    auto drain_one = [&]() -> bool {
+      // skip units without K work (they still produce a zero tile)
+      const int p = d % NPAIR;
+      if (!mbar_wait(filled(p), (d / NPAIR) & 1)) return false;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t rs[16], rb[16];
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+            : "=r"(rs[0]), "=r"(rs[1]), "=r"(rs[2]), "=r"(rs[3]), "=r"(rs[4]), "=r"(rs[5]), "=r"(rs[6]),
+              "=r"(rs[7]), "=r"(rs[8]), "=r"(rs[9]), "=r"(rs[10]), "=r"(rs[11]), "=r"(rs[12]), "=r"(rs[13]),
+              "=r"(rs[14]), "=r"(rs[15])
+            : "r"(taddr + (uint32_t)(BN * (2 * p + 1) + c0)));
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+            : "=r"(rb[0]), "=r"(rb[1]), "=r"(rb[2]), "=r"(rb[3]), "=r"(rb[4]), "=r"(rb[5]), "=r"(rb[6]),
+              "=r"(rb[7]), "=r"(rb[8]), "=r"(rb[9]), "=r"(rb[10]), "=r"(rb[11]), "=r"(rb[12]), "=r"(rb[13]),
+              "=r"(rb[14]), "=r"(rb[15])
+            : "r"(taddr + (uint32_t)(BN * (2 * p) + c0)));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) acc[c0 + jj] += __uint_as_float(rb[jj]) + __uint_as_float(rs[jj]);
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      mbar_arrive(drained(p));
+      ++d;
+      ++dks;
+      return true;
+    };
+    // Store the tile of unit dw (after its last stage is drained) and move on.
+    auto finish_units = [&]() {
+      while (du < units && dks >= dw.nk) {
+        const int row = dw.m0 + 32 * (warp & 3) + lane;
+        float* Cu = splits > 1 ? C + (long)dw.split * M * ldc : C;
+        const float* bu = splits > 1 ? nullptr : bias;
+        if (row < M) {
+          float* crow = Cu + (long)row * ldc + dw.n0;
+          const bool vec = (ldc % 4 == 0) && dw.n0 + BN <= N &&
+                           ((reinterpret_cast<uintptr_t>(crow) & 15) == 0);
+          if (vec) {
+#pragma unroll
+            for (int c = 0; c < BN; c += 4) {
+              float4 v = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
+              if (bu) {
+                v.x += bu[dw.n0 + c]; v.y += bu[dw.n0 + c + 1]; v.z += bu[dw.n0 + c + 2]; v.w += bu[dw.n0 + c + 3];
+              }
+              *reinterpret_cast<float4*>(crow + c) = v;
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < BN; ++c) {
+              const int n = dw.n0 + c;
+              if (n < N) crow[c] = acc[c] + (bu ? bu[n] : 0.0f);
+            }
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < BN; ++c) acc[c] = 0.0f;
+        du += gridDim.x;
+        dks = 0;
+        if (du < units) dw = unit_of<BN>(du, tiles_n, tiles, M, K, kchunk);
+      }
+    };
+    if (drainer) finish_units();
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      const Unit w = unit_of<BN>(u, tiles_n, tiles, M, K, kchunk);
+      for (int ks = 0; ks < w.nk; ++ks, ++i) {
         const int s = i % S;
         if (!mbar_wait(full(s), (i / S) & 1)) { ok = false; break; }
         float4* a = reinterpret_cast<float4*>(smem + s * L::kStage);
@@ -305,44 +406,19 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         mbar_arrive(ready(s));
-      }
-      if (drainer && i >= 1) {
-        const int d = i - 1, p = d % NPAIR;
-        if (!mbar_wait(filled(p), (d / NPAIR) & 1)) { ok = false; break; }
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-#pragma unroll
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-          uint32_t rs[16], rb[16];
-          asm volatile(
-              "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-              : "=r"(rs[0]), "=r"(rs[1]), "=r"(rs[2]), "=r"(rs[3]), "=r"(rs[4]), "=r"(rs[5]), "=r"(rs[6]),
-                "=r"(rs[7]), "=r"(rs[8]), "=r"(rs[9]), "=r"(rs[10]), "=r"(rs[11]), "=r"(rs[12]), "=r"(rs[13]),
-                "=r"(rs[14]), "=r"(rs[15])
-              : "r"(taddr + (uint32_t)(BN * (2 * p + 1) + c0)));
-          asm volatile(
-              "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-              : "=r"(rb[0]), "=r"(rb[1]), "=r"(rb[2]), "=r"(rb[3]), "=r"(rb[4]), "=r"(rb[5]), "=r"(rb[6]),
-                "=r"(rb[7]), "=r"(rb[8]), "=r"(rb[9]), "=r"(rb[10]), "=r"(rb[11]), "=r"(rb[12]), "=r"(rb[13]),
-                "=r"(rb[14]), "=r"(rb[15])
-              : "r"(taddr + (uint32_t)(BN * (2 * p) + c0)));
-          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-          for (int jj = 0; jj < 16; ++jj) acc[c0 + jj] += __uint_as_float(rb[jj]) + __uint_as_float(rs[jj]);
+        // Drain the previous stage (the tensor cores are already on this one).
+        if (drainer && d < i) {
+          if (!drain_one()) { ok = false; break; }
+          finish_units();
         }
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        mbar_arrive(drained(p));
       }
     }
-    if (drainer && ok) {
-      const int row = m0 + 32 * (warp & 3) + lane;
-      if (row < M) {
-        float* crow = C + (long)row * ldc;
-#pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          const int n = n0 + c;
-          if (n < N) crow[n] = acc[c] + (bias ? bias[n] : 0.0f);
-        }
+    if (drainer) {
+      while (ok && d < i) {
+        if (!drain_one()) { ok = false; break; }
+        finish_units();
       }
+      if (ok) finish_units();
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -431,8 +507,9 @@ int launch_tc(const TcGemmArgs& a, float* C, long ldc, const float* bias, int sp
   rc = B_MN ? make_map(&mb, a.B, a.K, a.N, a.ldb, 32, kBK, true)
             : make_map(&mb, a.B, a.N, a.K, a.ldb, kBK, kBN, false);
   if (rc) return rc;
-  dim3 grid(((a.M + kBM - 1) / kBM) * ((a.N + kBN - 1) / kBN), splits);
-  kern<<<grid, kThreads, LDefault::kBytes, stream>>>(ma, mb, C, ldc, bias, a.M, a.N, a.K, kchunk);
+  const int units = ((a.M + kBM - 1) / kBM) * ((a.N + kBN - 1) / kBN) * splits;
+  const int grid = units < sm_count(dev) ? units : sm_count(dev);
+  kern<<<grid, kThreads, LDefault::kBytes, stream>>>(ma, mb, C, ldc, bias, a.M, a.N, a.K, kchunk, splits);
   GRU_CUDA_TRY(cudaGetLastError());
   return GRU_OK;
 }
