@@ -486,7 +486,7 @@ __global__ void splitk_sum_kernel(const float* __restrict__ part, int S, int M, 
   }
 }
 
-constexpr int kBN = 64, kS = 4, kNPAIR = 4;
+constexpr int kBN = 128, kS = 3, kNPAIR = 2;
 using LDefault = Smem<kBN, kS>;
 
 template <bool A_MN, bool B_MN>
