@@ -112,7 +112,8 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_dyn(int n) {
-  if (n >= 2) cp_async_wait<2>();
+  if (n >= 3) cp_async_wait<3>();
+  else if (n == 2) cp_async_wait<2>();
   else if (n == 1) cp_async_wait<1>();
   else cp_async_wait<0>();
 }
@@ -224,11 +225,6 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
     const float* rg = ring + (t % pd) * ring_stride;
     if (t > 0) ok = mbar_wait_bounded(bar0 + 8 * cur, phase_parity(t));
     if (!ok) break;
-    // Past the wait every thread of the cluster has sent its step t-1 h
-    // values, and each of those depended on that thread's reads of ring slot
-    // (t-1) % pd, which this prefetch overwrites.
-    if (t + pd - 1 < T) issue(t + pd - 1);
-    else cp_async_commit();
 
     for (int b0 = 0; b0 < nb; b0 += R) {
       float2 acc[R][3];
@@ -254,7 +250,7 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
 #pragma unroll
         for (int q = 0; q < 3; ++q) part[((warp * R + s) * 3 + q) * 32 + lane] = acc[s][q].x + acc[s][q].y;
       }
-      if (b0 == 0) cp_async_wait_dyn(pd - 1);
+      if (b0 == 0) cp_async_wait_dyn(pd - 2);
       __syncthreads();
       // Every thread is past its wait on slot `cur`: re-arm it for step t+2.
       if (b0 == 0 && tid == 0 && t + 2 < T) mbar_expect_tx(bar0 + 8 * cur, bytes_per_step);
@@ -304,6 +300,12 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
       }
       if (b0 + R < nb) __syncthreads();  // `part` is reused by the next sub-chunk
     }
+    // Prefetch for step t+pd-1, off the critical path (the step's h values are
+    // sent).  It overwrites ring slot (t-1) % pd: past this step's wait every
+    // thread of the cluster has sent its step t-1 values, each of which
+    // depended on that thread's reads of the slot.
+    if (t + pd - 1 < T) issue(t + pd - 1);
+    else cp_async_commit();
   }
   cp_async_wait<0>();
   cluster.sync();  // no CTA leaves while a peer may still write into it
@@ -414,13 +416,9 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
     const int wslot = it & 1;
     if (it > 0) ok = mbar_wait_bounded(bar0 + 8 * rslot, phase_parity(it));
     if (!ok) break;
-    // Past the wait every CTA has sent its iteration it-1 partials, which
-    // follow (barrier) its reads of ring slot (it-1) % pd overwritten here.
-    if (it + pd - 1 < T) issue(it + pd - 1);
-    else cp_async_commit();
 
     for (int b0 = 0; b0 < nb; b0 += R) {
-      if (b0 == 0) cp_async_wait_dyn(pd - 1);
+      if (b0 == 0) cp_async_wait_dyn(pd - 2);
       __syncthreads();
       const int ns = min(R, nb - b0);
       for (int e = tid; e < ns * hcnt; e += nthr) {
@@ -499,6 +497,11 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
         }
       }
     }
+    // Prefetch for iteration it+pd-1, off the critical path.  It overwrites
+    // ring slot (it-1) % pd: past this iteration's wait every CTA has sent its
+    // iteration it-1 partials, which follow (barrier) its reads of the slot.
+    if (it + pd - 1 < T) issue(it + pd - 1);
+    else cp_async_commit();
   }
 
   // dh0 = g*z of iteration T-1 (t = 0) plus every CTA's partial product of
@@ -606,8 +609,8 @@ int finish_geometry(RecGeom* g, int device, bool fwd, SmemFn smem_of) {
     g->bc = bc;
     g->R = bc < kMaxRows ? bc : kMaxRows;
     g->bcp = ceil_div(bc, g->R) * g->R;
-    g->pd = 3;
-    if (smem_of(*g) > (size_t)max_smem) g->pd = 2;
+    g->pd = 4;  // prefetch issued at the end of step t for step t + pd - 1
+    while (g->pd > 2 && smem_of(*g) > (size_t)max_smem) --g->pd;
     if (smem_of(*g) <= (size_t)max_smem) break;
     if (bc <= 1) {
       set_error("recurrent kernel shared memory does not fit");
