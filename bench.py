@@ -126,7 +126,8 @@ def run_reference(args, world, rank):
         return 0
     from oracle.cpu_baseline import time_cpu_train_step
 
-    B = args.global_batch // world if args.global_batch else args.batch_per_gpu
+    # The whole job's batch (all ranks' shards), run on the host cores.
+    B = args.global_batch if args.global_batch else args.batch_per_gpu * world
     T, I, H = args.seq_len, args.input_size, args.hidden_size
     # One step of the full workload takes about a second on a many-core host;
     # cap the count so the whole run stays within a few minutes.
@@ -137,11 +138,12 @@ def run_reference(args, world, rank):
         "impl": "reference", "metric": METRIC, "value": r["value"], "unit": UNIT, "n_gpus": world,
         "steps": steps, "warmup": warm, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic N(0,1) x and target",
-        "config": {"workload": f"gru_train_step I={I} H={H} B={B} T={T} (rank-0 shard)", "global_batch": B,
+        "config": {"workload": f"gru_train_step I={I} H={H} T={T}, global batch {B} on the host CPU",
+                   "global_batch": B,
                    "seq_len": T, "input_size": I, "hidden_size": H, "layers": 1, "parallelism": "cpu"},
         "cpu_baseline": {"value": r["value"], "unit": UNIT, "cores": r["cores"], "kind": "reference",
                          "sample": f"torch.nn.GRU FP32 train step on host CPU ({r['cpu_model']}), "
-                                   f"full B={B},T={T} shard, {warm} warm-up + {steps} timed steps"},
+                                   f"full global B={B},T={T}, {warm} warm-up + {steps} timed steps"},
         "e2e": {"value": r["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
