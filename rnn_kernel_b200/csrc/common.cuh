@@ -46,6 +46,7 @@ struct RecGeom {
   // Shared-memory layout, offsets in floats from the dynamic base; every
   // region starts on a 16-byte boundary (float4 accesses).
   int off1, off2, off3;
+  int vec4;  // per-step input rows are 16-byte aligned (H, Hc multiples of 4)
   size_t smem;  // dynamic shared memory bytes per CTA
 };
 

@@ -106,6 +106,9 @@ __device__ __forceinline__ void fence_mbar_init() {
 __device__ __forceinline__ void cp_async4(float* smem_dst, const float* gmem_src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(smem_u32(smem_dst)), "l"(gmem_src));
 }
+__device__ __forceinline__ void cp_async16(float* smem_dst, const float* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(smem_dst)), "l"(gmem_src));
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
@@ -198,21 +201,33 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
     if (T > 1) mbar_expect_tx(bar0 + 8, bytes_per_step);  // slot 1 <- step 1
   }
 
-  auto issue = [&](int s) {
+  // Prefetch of step s's input gates into ring slot s % pd by the threads
+  // first, first + stride, ...: 16-byte copies when the rows are 16-byte
+  // aligned (H and Hc multiples of 4), else 4-byte copies.  No commit.
+  const bool vec4 = g.vec4 != 0;
+  auto issue = [&](int s, int first, int stride) {
     float* dst = ring + (s % pd) * ring_stride;
-    const int n = nb * 3 * hcnt;
-    for (int e = tid; e < n; e += nthr) {
-      const int jl = e % hcnt;
-      const int r = e / hcnt;
-      const int gi = r % 3, b = r / 3;
-      cp_async4(dst + (b * 3 + gi) * Hc + jl,
-                a.G + ((size_t)(b_begin + b) * T + s) * 3 * H + gi * H + j0 + jl);
+    const float* src = a.G + ((size_t)b_begin * T + s) * 3 * H + j0;
+    const size_t bstride = (size_t)T * 3 * H;
+    if (vec4) {
+      const int h4 = hcnt >> 2, n = nb * 3 * h4;
+      for (int e = first; e < n; e += stride) {
+        const int r = e / h4, jl = 4 * (e - r * h4);
+        const int b = r / 3, gi = r - 3 * b;
+        cp_async16(dst + r * Hc + jl, src + b * bstride + gi * H + jl);
+      }
+    } else {
+      const int n = nb * 3 * hcnt;
+      for (int e = first; e < n; e += stride) {
+        const int r = e / hcnt, jl = e - r * hcnt;
+        const int b = r / 3, gi = r - 3 * b;
+        cp_async4(dst + r * Hc + jl, src + b * bstride + gi * H + jl);
+      }
     }
-    cp_async_commit();
   };
   for (int s = 0; s < pd - 1; ++s) {
-    if (s < T) issue(s);
-    else cp_async_commit();
+    if (s < T) issue(s, tid, nthr);
+    cp_async_commit();
   }
 
   const uint32_t hbuf_u32 = smem_u32(hbuf);
@@ -256,6 +271,13 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
       if (b0 == 0 && tid == 0 && t + 2 < T) mbar_expect_tx(bar0 + 8 * cur, bytes_per_step);
 
       const int ns = min(R, nb - b0);
+      // Threads without a pointwise item in the last sub-chunk issue the
+      // prefetch for step t+pd-1 meanwhile (it overwrites ring slot
+      // (t-1) % pd: past this step's wait every thread of the cluster has
+      // sent its step t-1 values, each of which depended on its reads of that
+      // slot).
+      const int nact = ns * hcnt;
+      if (b0 + R >= nb && nact < nthr && tid >= nact && t + pd - 1 < T) issue(t + pd - 1, tid - nact, nthr - nact);
       for (int e = tid; e < ns * hcnt; e += nthr) {
         const int s = e / hcnt, jl = e - s * hcnt;
         const int b = b0 + s, j = j0 + jl;
@@ -300,12 +322,12 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
       }
       if (b0 + R < nb) __syncthreads();  // `part` is reused by the next sub-chunk
     }
-    // Prefetch for step t+pd-1, off the critical path (the step's h values are
-    // sent).  It overwrites ring slot (t-1) % pd: past this step's wait every
-    // thread of the cluster has sent its step t-1 values, each of which
-    // depended on that thread's reads of the slot.
-    if (t + pd - 1 < T) issue(t + pd - 1);
-    else cp_async_commit();
+    // Every thread had a pointwise item: prefetch now, after the sends.
+    {
+      const int ns_last = nb - ((nb - 1) / R) * R;
+      if (ns_last * hcnt >= nthr && t + pd - 1 < T) issue(t + pd - 1, tid, nthr);
+    }
+    cp_async_commit();
   }
   cp_async_wait<0>();
   cluster.sync();  // no CTA leaves while a peer may still write into it
@@ -375,28 +397,34 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
   }
 
   // Ring entry q: 0 dout, 1 r, 2 z, 3 n, 4 hn (= W_hn.h + b_hn), 5 h_prev.
-  auto issue = [&](int it) {
+  // Prefetch of iteration it's inputs into ring slot it % pd by the threads
+  // first, first + stride, ...; 16-byte copies when rows are 16-byte aligned.
+  // No commit.
+  const bool vec4 = g.vec4 != 0;
+  auto issue = [&](int it, int first, int stride) {
     const int s = T - 1 - it;
     float* dst = ring + (it % pd) * ring_stride;
-    const int n = nb * 6 * hcnt;
-    for (int e = tid; e < n; e += nthr) {
-      const int jl = e % hcnt;
-      const int r = e / hcnt;
-      const int q = r % 6, b = r / 6;
+    const int w = vec4 ? 4 : 1;
+    const int hw = hcnt / w, n = nb * 6 * hw;
+    for (int e = first; e < n; e += stride) {
+      const int r = e / hw, jl = w * (e - r * hw);
+      const int b = r / 6, q = r - 6 * b;
       const size_t row = (size_t)(b_begin + b) * T + s;
-      float* d = dst + (b * 6 + q) * Hc + jl;
-      if (q == 0) {
-        if (a.dout != nullptr) cp_async4(d, a.dout + row * H + j0 + jl);
-        else *d = 0.0f;
+      float* d = dst + r * Hc + jl;
+      const float* src = q == 0 ? (a.dout ? a.dout + row * H + j0 + jl : nullptr)
+                                : a.stash + row * 5 * H + (q - 1) * H + j0 + jl;
+      if (src == nullptr) {
+        for (int v = 0; v < w; ++v) d[v] = 0.0f;
+      } else if (vec4) {
+        cp_async16(d, src);
       } else {
-        cp_async4(d, a.stash + row * 5 * H + (q - 1) * H + j0 + jl);
+        cp_async4(d, src);
       }
     }
-    cp_async_commit();
   };
   for (int it = 0; it < pd - 1; ++it) {
-    if (it < T) issue(it);
-    else cp_async_commit();
+    if (it < T) issue(it, tid, nthr);
+    cp_async_commit();
   }
 
   const int kown = (k < H) ? k / Hc : 0;
@@ -421,6 +449,12 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
       if (b0 == 0) cp_async_wait_dyn(pd - 2);
       __syncthreads();
       const int ns = min(R, nb - b0);
+      // Threads without a pointwise item in the last sub-chunk issue the
+      // prefetch for iteration it+pd-1 meanwhile (it overwrites ring slot
+      // (it-1) % pd: past this iteration's wait every CTA has sent its
+      // iteration it-1 partials, which follow (barrier) its reads of the slot).
+      const int nact = ns * hcnt;
+      if (b0 + R >= nb && nact < nthr && tid >= nact && it + pd - 1 < T) issue(it + pd - 1, tid - nact, nthr - nact);
       for (int e = tid; e < ns * hcnt; e += nthr) {
         const int s = e / hcnt, jl = e - s * hcnt;
         const int b = b0 + s, j = j0 + jl;
@@ -497,11 +531,12 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
         }
       }
     }
-    // Prefetch for iteration it+pd-1, off the critical path.  It overwrites
-    // ring slot (it-1) % pd: past this iteration's wait every CTA has sent its
-    // iteration it-1 partials, which follow (barrier) its reads of the slot.
-    if (it + pd - 1 < T) issue(it + pd - 1);
-    else cp_async_commit();
+    // Every thread had a pointwise item: prefetch now, after the sends.
+    {
+      const int ns_last = nb - ((nb - 1) / R) * R;
+      if (ns_last * hcnt >= nthr && it + pd - 1 < T) issue(it + pd - 1, tid, nthr);
+    }
+    cp_async_commit();
   }
 
   // dh0 = g*z of iteration T-1 (t = 0) plus every CTA's partial product of
@@ -530,6 +565,7 @@ int base_geometry(int B, int T, int H, RecGeom* g) {
   g->C = ceil_div(H, 32);
   g->Hc = ceil_div(H, g->C);
   g->nw = g->C;
+  g->vec4 = (H % 4 == 0 && g->Hc % 4 == 0) ? 1 : 0;
   return GRU_OK;
 }
 
@@ -676,14 +712,18 @@ int launch_rec_forward(const float* G, const float* h0, const float* w_hh, const
                        float* out, float* hn, float* stash, const RecGeom& g,
                        cudaStream_t stream) {
   FwdArgs a{G, h0, w_hh, b_hh, out, hn, stash};
-  return launch_clusters(kernel_for(true, g.R), a, g, stream, kKindFwdRecurrent);
+  RecGeom gg = g;
+  if (reinterpret_cast<uintptr_t>(G) & 15) gg.vec4 = 0;  // 16-byte copies need an aligned base
+  return launch_clusters(kernel_for(true, gg.R), a, gg, stream, kKindFwdRecurrent);
 }
 
 int launch_rec_backward(const float* dout, const float* dhn, const float* w_hh,
                         const float* stash, float* dGi, int ldgi, float* dGh, float* dh0,
                         const RecGeom& g, cudaStream_t stream) {
   BwdArgs a{dout, dhn, w_hh, stash, dGi, ldgi, dGh, dh0};
-  return launch_clusters(kernel_for(false, g.R), a, g, stream, kKindBwdRecurrent);
+  RecGeom gg = g;
+  if ((reinterpret_cast<uintptr_t>(dout) | reinterpret_cast<uintptr_t>(stash)) & 15) gg.vec4 = 0;
+  return launch_clusters(kernel_for(false, gg.R), a, gg, stream, kKindBwdRecurrent);
 }
 
 }  // namespace gru
