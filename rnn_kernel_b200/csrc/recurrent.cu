@@ -360,7 +360,11 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
   const int H = g.H, T = g.T, Hc = g.Hc, bcp = g.bcp, pd = g.pd, C = g.C;
   const int j0 = c * Hc;
   const int hcnt = max(1, min(Hc, H - j0));
-  const int k = warp * 32 + lane;  // W_hh column this thread owns in the GEMV
+  // GEMV mapping: lane l of warp w owns the W_hh columns k0 = 32w + 2(l & 15)
+  // and k0 + 1 for the half jh = l >> 4 of this CTA's units (16 each).
+  const int jh = lane >> 4;
+  const int k0 = warp * 32 + 2 * (lane & 15);
+  const int ksend = k0 + jh;  // the column whose finished partial this lane sends
 
   extern __shared__ __align__(16) float smem[];
   __shared__ __align__(8) unsigned long long mbar[2];
@@ -371,19 +375,18 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
   const int ring_stride = bcp * 6 * Hc;
   const int red_slot = C * bcp * Hc;
 
-  // W_hh[g*H + j0 + j][k] for j < Hc, as pairs (j, j+1) for FFMA2.
+  // (W_hh[g*H + j][k0], W_hh[g*H + j][k0 + 1]) for the 16 units j of half jh,
+  // as pairs over the two columns for FFMA2.
   float2 wr[16], wz[16], wn[16];
 #pragma unroll
   for (int jj = 0; jj < 16; ++jj) {
-    const int j = 2 * jj;
-    const bool v0 = j < hcnt && j0 + j < H && k < H;
-    const bool v1 = j + 1 < hcnt && j0 + j + 1 < H && k < H;
-    wr[jj] = make_float2(v0 ? a.w_hh[(size_t)(j0 + j) * H + k] : 0.f,
-                         v1 ? a.w_hh[(size_t)(j0 + j + 1) * H + k] : 0.f);
-    wz[jj] = make_float2(v0 ? a.w_hh[(size_t)(H + j0 + j) * H + k] : 0.f,
-                         v1 ? a.w_hh[(size_t)(H + j0 + j + 1) * H + k] : 0.f);
-    wn[jj] = make_float2(v0 ? a.w_hh[(size_t)(2 * H + j0 + j) * H + k] : 0.f,
-                         v1 ? a.w_hh[(size_t)(2 * H + j0 + j + 1) * H + k] : 0.f);
+    const int jl = 16 * jh + jj;
+    const bool vj = jl < hcnt && j0 + jl < H;
+    const bool v0 = vj && k0 < H, v1 = vj && k0 + 1 < H;
+    const size_t rr = (size_t)(j0 + jl) * H, rz = (size_t)(H + j0 + jl) * H, rn = (size_t)(2 * H + j0 + jl) * H;
+    wr[jj] = make_float2(v0 ? a.w_hh[rr + k0] : 0.f, v1 ? a.w_hh[rr + k0 + 1] : 0.f);
+    wz[jj] = make_float2(v0 ? a.w_hh[rz + k0] : 0.f, v1 ? a.w_hh[rz + k0 + 1] : 0.f);
+    wn[jj] = make_float2(v0 ? a.w_hh[rn + k0] : 0.f, v1 ? a.w_hh[rn + k0 + 1] : 0.f);
   }
 
   for (int e = tid; e < 2 * red_slot; e += nthr) red[e] = 0.0f;
@@ -429,8 +432,8 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
     cp_async_commit();
   }
 
-  const int kown = (k < H) ? k / Hc : 0;
-  const int kl = (k < H) ? k - kown * Hc : 0;
+  const int kown = (ksend < H) ? ksend / Hc : 0;
+  const int kl = (ksend < H) ? ksend - kown * Hc : 0;
   // This thread's partial for row b of slot s lands in red[s][c][b][kl] of
   // CTA kown and completes bytes on that CTA's mbarrier s.
   const uint32_t dst_base = mapa_u32(smem_u32(red) + 4u * (uint32_t)(c * bcp * Hc + kl), kown);
@@ -501,35 +504,44 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
       if (b0 == 0 && tid == 0 && it > 0 && it + 2 <= T) mbar_expect_tx(bar0 + 8 * rslot, bytes_per_step);
       if (b0 == 0 && tid == 0 && it == 0 && T >= 2) mbar_expect_tx(bar0 + 8, bytes_per_step);
 
-      if (k < H) {
+      {
         const uint32_t dst = dst_base + 4u * (uint32_t)(wslot * red_slot + b0 * Hc);
         const uint32_t dbar = dst_bar0 + 8u * wslot;
-        float2 acc[R][3];
+        float2 acc[R][3];  // (column k0, column k0 + 1) partials per gate
 #pragma unroll
         for (int s = 0; s < R; ++s) acc[s][0] = acc[s][1] = acc[s][2] = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
+        for (int jj = 0; jj < 16; jj += 4) {
 #pragma unroll
           for (int s = 0; s < R; ++s) {
-            const float* d = dgs + s * 3 * 32 + j;
+            const float* d = dgs + s * 3 * 32 + 16 * jh + jj;
             const float4 vr = *reinterpret_cast<const float4*>(d);
             const float4 vz = *reinterpret_cast<const float4*>(d + 32);
             const float4 vn = *reinterpret_cast<const float4*>(d + 64);
-            acc[s][0] = __ffma2_rn(make_float2(vr.x, vr.y), wr[j / 2], acc[s][0]);
-            acc[s][1] = __ffma2_rn(make_float2(vz.x, vz.y), wz[j / 2], acc[s][1]);
-            acc[s][2] = __ffma2_rn(make_float2(vn.x, vn.y), wn[j / 2], acc[s][2]);
-            acc[s][0] = __ffma2_rn(make_float2(vr.z, vr.w), wr[j / 2 + 1], acc[s][0]);
-            acc[s][1] = __ffma2_rn(make_float2(vz.z, vz.w), wz[j / 2 + 1], acc[s][1]);
-            acc[s][2] = __ffma2_rn(make_float2(vn.z, vn.w), wn[j / 2 + 1], acc[s][2]);
+            acc[s][0] = __ffma2_rn(make_float2(vr.x, vr.x), wr[jj], acc[s][0]);
+            acc[s][1] = __ffma2_rn(make_float2(vz.x, vz.x), wz[jj], acc[s][1]);
+            acc[s][2] = __ffma2_rn(make_float2(vn.x, vn.x), wn[jj], acc[s][2]);
+            acc[s][0] = __ffma2_rn(make_float2(vr.y, vr.y), wr[jj + 1], acc[s][0]);
+            acc[s][1] = __ffma2_rn(make_float2(vz.y, vz.y), wz[jj + 1], acc[s][1]);
+            acc[s][2] = __ffma2_rn(make_float2(vn.y, vn.y), wn[jj + 1], acc[s][2]);
+            acc[s][0] = __ffma2_rn(make_float2(vr.z, vr.z), wr[jj + 2], acc[s][0]);
+            acc[s][1] = __ffma2_rn(make_float2(vz.z, vz.z), wz[jj + 2], acc[s][1]);
+            acc[s][2] = __ffma2_rn(make_float2(vn.z, vn.z), wn[jj + 2], acc[s][2]);
+            acc[s][0] = __ffma2_rn(make_float2(vr.w, vr.w), wr[jj + 3], acc[s][0]);
+            acc[s][1] = __ffma2_rn(make_float2(vz.w, vz.w), wz[jj + 3], acc[s][1]);
+            acc[s][2] = __ffma2_rn(make_float2(vn.w, vn.w), wn[jj + 3], acc[s][2]);
           }
         }
 #pragma unroll
         for (int s = 0; s < R; ++s) {
-          if (s < ns) {
-            const float v = (acc[s][0].x + acc[s][0].y) + (acc[s][1].x + acc[s][1].y) +
-                            (acc[s][2].x + acc[s][2].y);
-            st_async_f32(dst + 4u * (uint32_t)(s * Hc), v, dbar);
-          }
+          // this half's sums for columns k0 and k0+1; the other half (lane ^ 16)
+          // holds the rest of the same two columns
+          const float c0 = acc[s][0].x + acc[s][1].x + acc[s][2].x;
+          const float c1 = acc[s][0].y + acc[s][1].y + acc[s][2].y;
+          const float o0 = __shfl_xor_sync(0xffffffffu, c0, 16);
+          const float o1 = __shfl_xor_sync(0xffffffffu, c1, 16);
+          const float v = jh == 0 ? c0 + o0 : o1 + c1;  // column ksend = k0 + jh
+          if (s < ns && ksend < H) st_async_f32(dst + 4u * (uint32_t)(s * Hc), v, dbar);
         }
       }
     }
