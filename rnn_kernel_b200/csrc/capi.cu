@@ -121,7 +121,7 @@ BwdLayout bwd_layout(int B, int T, int I, int H, int device) {
   }
   off = align_up(off + g, kAlign);
   l.col = off;
-  off = align_up(off + colsum_ws_bytes(BT, 3 * H), kAlign);
+  off = align_up(off + bias_grad_ws_bytes(H), kAlign);
   l.total = off;
   return l;
 }
@@ -308,8 +308,7 @@ int gru_backward(const float* dout, const float* dhn, const float* x, const floa
     TcGemmArgs a3{dGi, l.ldgi, wt, l.ldgi, dx, I, nullptr, BT, I, H3};
     if ((rc = tc_gemm(a3, stream, kKindGradGemm))) return rc;
   }
-  if ((rc = colsum(dGi, BT, H3, l.ldgi, db_ih, ws + l.col, stream))) return rc;
-  if ((rc = colsum(dGh, BT, H3, l.ldgi, db_hh, ws + l.col, stream))) return rc;
+  if ((rc = bias_grads(dGi, dGh, BT, H, l.ldgi, db_ih, db_hh, ws + l.col, stream))) return rc;
   return GRU_OK;
 }
 

@@ -107,10 +107,12 @@ int read_gemm_status(int reset, int* status);
 int pad_rows(const float* src, long rows, int cols, float* dst, int ldd, cudaStream_t stream);
 int transpose(const float* src, int rows, int cols, float* dst, int ldd, cudaStream_t stream);
 
-// Column sums of a [rows, cols] matrix with row stride ld into out[cols]
-// (fp64 accumulation, deterministic two-pass).  ws needs colsum_ws_bytes().
-size_t colsum_ws_bytes(long rows, int cols);
-int colsum(const float* X, long rows, int cols, long ld, float* out, void* ws, cudaStream_t stream);
+// Bias gradients db_ih = colsum(dG_ih), db_hh = colsum(dG_hh) over `rows`
+// rows of row stride ld (FP64 accumulation, deterministic two-pass; the
+// shared r/z columns are summed once).  ws needs bias_grad_ws_bytes(H).
+size_t bias_grad_ws_bytes(int H);
+int bias_grads(const float* dgi, const float* dgh, long rows, int H, long ld, float* db_ih, float* db_hh, void* ws,
+               cudaStream_t stream);
 
 int sm_count(int device);
 

@@ -96,21 +96,38 @@ int splits_for(int M, int N, int K, int device) {
   return S;
 }
 
-__global__ void colsum_partial_kernel(const float* X, long rows, int cols, long ld, long rchunk, double* part) {
+// Bias gradients.  dG_ih = [dr, dz, dn_pre] and dG_hh = [dr, dz, dhn] share
+// their r and z columns, so one pass sums the 3H columns of dG_ih and the n
+// block of dG_hh (virtual columns 3H .. 4H): db_ih = cols [0, 3H),
+// db_hh = [cols 0 .. 2H, cols 3H .. 4H).
+__global__ void bias_grad_partial_kernel(const float* __restrict__ dgi, const float* __restrict__ dgh, long rows,
+                                         int H, long ld, long rchunk, double* __restrict__ part) {
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
-  if (col >= cols) return;
+  if (col >= 4 * H) return;
+  const float* X = col < 3 * H ? dgi + col : dgh + (col - H);  // dG_hh n block = its columns 2H .. 3H
   const long r0 = blockIdx.y * rchunk, r1 = min(rows, r0 + rchunk);
-  double s = 0.0;
-  for (long r = r0; r < r1; ++r) s += X[r * ld + col];
-  part[(long)blockIdx.y * cols + col] = s;
+  double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
+  long r = r0;
+  for (; r + 4 <= r1; r += 4) {
+    s0 += X[r * ld];
+    s1 += X[(r + 1) * ld];
+    s2 += X[(r + 2) * ld];
+    s3 += X[(r + 3) * ld];
+  }
+  for (; r < r1; ++r) s0 += X[r * ld];
+  part[(long)blockIdx.y * 4 * H + col] = (s0 + s1) + (s2 + s3);
 }
 
-__global__ void colsum_final_kernel(const double* part, int nchunks, int cols, float* out) {
+__global__ void bias_grad_final_kernel(const double* __restrict__ part, int nchunks, int H, float* __restrict__ db_ih,
+                                       float* __restrict__ db_hh) {
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
-  if (col >= cols) return;
+  if (col >= 4 * H) return;
   double s = 0.0;
-  for (int z = 0; z < nchunks; ++z) s += part[(long)z * cols + col];
-  out[col] = (float)s;
+  for (int z = 0; z < nchunks; ++z) s += part[(long)z * 4 * H + col];
+  const float v = (float)s;
+  if (col < 3 * H) db_ih[col] = v;
+  if (col < 2 * H) db_hh[col] = v;
+  else if (col >= 3 * H) db_hh[col - H] = v;
 }
 
 constexpr int kColChunks = 256;
@@ -192,17 +209,18 @@ int gemm(const GemmArgs& a, void* ws, size_t ws_bytes, int device, cudaStream_t 
                : gemm_impl<float>(a, ws, ws_bytes, device, stream, kind);
 }
 
-size_t colsum_ws_bytes(long rows, int cols) { return sizeof(double) * (size_t)kColChunks * cols; }
+size_t bias_grad_ws_bytes(int H) { return sizeof(double) * (size_t)kColChunks * 4 * H; }
 
-int colsum(const float* X, long rows, int cols, long ld, float* out, void* ws, cudaStream_t stream) {
-  if (cols <= 0) return GRU_OK;
+int bias_grads(const float* dgi, const float* dgh, long rows, int H, long ld, float* db_ih, float* db_hh, void* ws,
+               cudaStream_t stream) {
+  if (H <= 0) return GRU_OK;
   const long rchunk = (rows + kColChunks - 1) / kColChunks;
   double* part = static_cast<double*>(ws);
-  dim3 grid(ceil_div(cols, 128), kColChunks);
+  dim3 grid(ceil_div(4 * H, 128), kColChunks);
   LaunchScope scope(kKindColsum, stream, 2);
-  colsum_partial_kernel<<<grid, 128, 0, stream>>>(X, rows, cols, ld, rchunk > 0 ? rchunk : 1, part);
+  bias_grad_partial_kernel<<<grid, 128, 0, stream>>>(dgi, dgh, rows, H, ld, rchunk > 0 ? rchunk : 1, part);
   GRU_CUDA_TRY(cudaGetLastError());
-  colsum_final_kernel<<<ceil_div(cols, 128), 128, 0, stream>>>(part, kColChunks, cols, out);
+  bias_grad_final_kernel<<<ceil_div(4 * H, 128), 128, 0, stream>>>(part, kColChunks, H, db_ih, db_hh);
   GRU_CUDA_TRY(cudaGetLastError());
   return GRU_OK;
 }
