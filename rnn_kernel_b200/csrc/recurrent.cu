@@ -240,8 +240,10 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
     const int cur = t & 1, nxt = cur ^ 1;
     const float* hcur = hbuf + cur * slot_stride;
     const float* rg = ring + (t % pd) * ring_stride;
-    if (t > 0) ok = mbar_wait_bounded(bar0 + 8 * cur, phase_parity(t));
-    if (!ok) break;
+    // After an expired wait (recorded in the status word) this thread stops
+    // waiting but still runs every remaining barrier, so no thread of the CTA
+    // or cluster is left behind at one; the results are then invalid.
+    if (t > 0 && ok) ok = mbar_wait_bounded(bar0 + 8 * cur, phase_parity(t));
 
     for (int b0 = 0; b0 < nb; b0 += R) {
       float2 acc[R][3];
@@ -447,8 +449,9 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
     const int rslot = (it + 1) & 1;  // partials written at iteration it-1
     const float* rin = red + rslot * red_slot;
     const int wslot = it & 1;
-    if (it > 0) ok = mbar_wait_bounded(bar0 + 8 * rslot, phase_parity(it));
-    if (!ok) break;
+    // After an expired wait (recorded in the status word) this thread stops
+    // waiting but still runs every remaining barrier; results are then invalid.
+    if (it > 0 && ok) ok = mbar_wait_bounded(bar0 + 8 * rslot, phase_parity(it));
 
     for (int b0 = 0; b0 < nb; b0 += R) {
       if (b0 == 0) cp_async_wait_dyn(pd - 2);
