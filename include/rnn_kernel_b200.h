@@ -113,6 +113,13 @@ int gru_forward_inference_noalloc(const float* x, const float* h0, const float* 
  * were grid.sync() calls with no bound. */
 int gru_device_status(int reset);
 
+/* Failure-path self-test (no reference counterpart): launches one CTA that
+ * waits, through the same bounded-wait routine the time loops use, on an
+ * mbarrier phase that nothing completes, with a limit of limit_ms (1..10000).
+ * It must return with *result (a device int) = 0 and GRU_STATUS_WAIT_TIMEOUT
+ * set in the status word, leaving the context usable; no fault, no trap. */
+int gru_selftest_wait_timeout(int limit_ms, int* result, void* stream);
+
 /* Number of kernels this library has launched in this process. */
 unsigned long long gru_launch_count(void);
 

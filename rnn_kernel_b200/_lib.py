@@ -30,6 +30,7 @@ SIGNATURES = {
     "gru_backward": (_int, [_c_float_p] * 12 + [ctypes.c_void_p, _size_t] + [_int] * 4 + [ctypes.c_void_p]),
     "gru_forward_inference_noalloc": (_int, [_c_float_p] * 8 + [_int] * 4 + [ctypes.c_void_p]),
     "gru_device_status": (_int, [_int]),
+    "gru_selftest_wait_timeout": (_int, [_int, ctypes.c_void_p, ctypes.c_void_p]),
     "gru_launch_count": (ctypes.c_ulonglong, []),
     "gru_timing_enable": (_int, [_int]),
     "gru_timing_collect": (_int, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int), _int]),

@@ -171,6 +171,15 @@ int gru_device_status(int reset) {
   return st | st2;
 }
 
+int gru_selftest_wait_timeout(int limit_ms, int* result, void* stream) {
+  clear_error();
+  if (limit_ms < 1 || limit_ms > 10000 || result == nullptr) {
+    set_error("gru_selftest_wait_timeout: need 1 <= limit_ms <= 10000 and a result pointer");
+    return GRU_ERR_INVALID;
+  }
+  return wait_probe((unsigned long long)limit_ms * 1000000ull, result, static_cast<cudaStream_t>(stream));
+}
+
 size_t gru_stash_bytes(int B, int T, int H) {
   if (B <= 0 || T <= 0 || H <= 0) return 0;
   return sizeof(float) * (size_t)B * T * 5 * H;

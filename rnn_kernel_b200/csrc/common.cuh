@@ -54,6 +54,7 @@ constexpr int kMaxRows = 8;     // largest GEMV sub-chunk (batch rows)
 constexpr int kMaxCluster = 8;  // CTAs per cluster for H <= 256
 
 int read_device_status(int reset, int* status);
+int wait_probe(unsigned long long limit_ns, int* result_dev, cudaStream_t stream);
 int rec_forward_geometry(int B, int T, int H, int device, RecGeom* g);
 int rec_backward_geometry(int B, int T, int H, int device, RecGeom* g);
 

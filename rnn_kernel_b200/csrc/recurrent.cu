@@ -82,13 +82,14 @@ __device__ __forceinline__ unsigned long long global_ns() {
 }
 // Bounded wait: false (and the timeout recorded) if the phase did not
 // complete within kWaitLimitNs.
-__device__ __noinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+__device__ __noinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
+                                               unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   for (;;) {
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (global_ns() - t0 > kWaitLimitNs) {
+    if (global_ns() - t0 > limit_ns) {
       atomicOr(&g_device_status, GRU_STATUS_WAIT_TIMEOUT);
       return false;
     }
@@ -704,6 +705,26 @@ int launch_clusters(const void* kernel, const Args& a, const RecGeom& g, cudaStr
 }
 
 }  // namespace
+
+// Self-test of the bounded wait: one CTA waits on an mbarrier phase that
+// nothing ever completes, with a limit of limit_ns, and must come back with
+// the timeout recorded in the status word instead of hanging.
+__global__ void wait_probe_kernel(unsigned long long limit_ns, int* result) {
+  __shared__ __align__(8) unsigned long long bar;
+  const uint32_t b = smem_u32(&bar);
+  if (threadIdx.x == 0) mbar_init(b, 1);
+  __syncthreads();
+  const bool ok = mbar_wait_bounded(b, 0, limit_ns);
+  __syncthreads();
+  if (threadIdx.x == 0) *result = ok ? 1 : 0;
+}
+
+int wait_probe(unsigned long long limit_ns, int* result_dev, cudaStream_t stream) {
+  LaunchScope scope(kKindFwdRecurrent, stream);
+  wait_probe_kernel<<<1, 32, 0, stream>>>(limit_ns, result_dev);
+  GRU_CUDA_TRY(cudaGetLastError());
+  return GRU_OK;
+}
 
 int read_device_status(int reset, int* status) {
   GRU_CUDA_TRY(cudaDeviceSynchronize());
