@@ -160,7 +160,7 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
   extern __shared__ __align__(16) float smem[];
   __shared__ __align__(8) unsigned long long mbar[2];
   float* hbuf = smem;                          // [2][bcp][Kp]
-  float* part = smem + g.off1;                 // [nw][R][3][32]
+  float* part = smem + g.off1;                 // [R][3][32 units][8 warp slots]
   float* ring = smem + g.off2;                 // [pd][bcp][3][Hc]
   float* bsl = smem + g.off3;                  // [3][Hc] this CTA's slice of b_hh
   const int ring_stride = bcp * 3 * Hc;
@@ -185,7 +185,7 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
   }
 
   for (int e = tid; e < 2 * slot_stride; e += nthr) hbuf[e] = 0.0f;
-  for (int e = tid; e < g.nw * R * 3 * 32; e += nthr) part[e] = 0.0f;
+  for (int e = tid; e < R * 3 * 32 * 8; e += nthr) part[e] = 0.0f;  // slots of absent warps stay 0
   for (int e = tid; e < 3 * Hc; e += nthr) {
     const int q = e / Hc, jl = e - q * Hc;
     bsl[e] = jl < hcnt ? a.b_hh[q * H + j0 + jl] : 0.0f;
@@ -265,10 +265,14 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
           acc[s][2] = __ffma2_rn(wn[kk / 2 + 1], h23, acc[s][2]);
         }
       }
+      // Partial of warp w for (row s, gate q, unit lane) goes to slot
+      // (w + lane/4) % 8 of that unit's 8-float row: conflict-free stores, and
+      // the pointwise thread reads the 8 partials with two float4 loads.
+      const int slot = (warp + (lane >> 2)) & 7;
 #pragma unroll
       for (int s = 0; s < R; ++s) {
 #pragma unroll
-        for (int q = 0; q < 3; ++q) part[((warp * R + s) * 3 + q) * 32 + lane] = acc[s][q].x + acc[s][q].y;
+        for (int q = 0; q < 3; ++q) part[((s * 3 + q) * 32 + lane) * 8 + slot] = acc[s][q].x + acc[s][q].y;
       }
       if (b0 == 0) cp_async_wait_dyn(pd - 2);
       __syncthreads();
@@ -286,22 +290,11 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
       for (int e = tid; e < ns * hcnt; e += nthr) {
         const int s = e / hcnt, jl = e - s * hcnt;
         const int b = b0 + s, j = j0 + jl;
-        float ar = bsl[jl], az = bsl[Hc + jl], an = bsl[2 * Hc + jl];
-        float pr[kMaxCluster], pz[kMaxCluster], pn[kMaxCluster];
-#pragma unroll
-        for (int w = 0; w < kMaxCluster; ++w) {
-          const float* p = part + ((w * R + s) * 3) * 32 + jl;
-          const bool v = w < g.nw;
-          pr[w] = v ? p[0] : 0.0f;
-          pz[w] = v ? p[32] : 0.0f;
-          pn[w] = v ? p[64] : 0.0f;
-        }
-#pragma unroll
-        for (int w = 0; w < kMaxCluster; ++w) {
-          ar += pr[w];
-          az += pz[w];
-          an += pn[w];
-        }
+        const float4* pp = reinterpret_cast<const float4*>(part + ((s * 3) * 32 + jl) * 8);
+        const float4 r0 = pp[0], r1 = pp[1], z0 = pp[64], z1 = pp[65], n0 = pp[128], n1 = pp[129];
+        const float ar = bsl[jl] + (((r0.x + r0.y) + (r0.z + r0.w)) + ((r1.x + r1.y) + (r1.z + r1.w)));
+        const float az = bsl[Hc + jl] + (((z0.x + z0.y) + (z0.z + z0.w)) + ((z1.x + z1.y) + (z1.z + z1.w)));
+        const float an = bsl[2 * Hc + jl] + (((n0.x + n0.y) + (n0.z + n0.w)) + ((n1.x + n1.y) + (n1.z + n1.w)));
         const float* gi = rg + (b * 3) * Hc + jl;
         const float r = sigmoidf_acc(gi[0] + ar);
         const float z = sigmoidf_acc(gi[Hc] + az);
@@ -593,7 +586,7 @@ inline int round4(size_t v) { return (int)((v + 3) / 4 * 4); }
 size_t fwd_smem(RecGeom& g) {
   const int Kp = g.nw * 32;
   g.off1 = round4((size_t)2 * g.bcp * Kp);
-  g.off2 = g.off1 + round4((size_t)g.nw * g.R * 3 * 32);
+  g.off2 = g.off1 + round4((size_t)g.R * 3 * 32 * 8);
   g.off3 = g.off2 + round4((size_t)g.pd * g.bcp * 3 * g.Hc);
   return sizeof(float) * (size_t)(g.off3 + round4((size_t)3 * g.Hc));
 }
