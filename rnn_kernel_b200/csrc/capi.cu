@@ -78,23 +78,21 @@ FwdLayout fwd_layout(int B, int T, int I, int H) {
   size_t off = 0;
   l.g = off;
   off = align_up(off + sizeof(float) * BT * 3 * H, kAlign);
-  if (l.pad) {
-    l.xp = off;
-    off = align_up(off + sizeof(float) * BT * pad4(I), kAlign);
-    l.wp = off;
-    off = align_up(off + sizeof(float) * (size_t)3 * H * pad4(I), kAlign);
-  }
+  // Room for 16-byte-stride copies of x and W_ih (I not a multiple of 4, or
+  // caller buffers not 16-byte aligned).
+  l.xp = off;
+  off = align_up(off + sizeof(float) * BT * pad4(I), kAlign);
+  l.wp = off;
+  off = align_up(off + sizeof(float) * (size_t)3 * H * pad4(I), kAlign);
   l.total = off;
   return l;
 }
 
-// dW products run on the tensor cores when h_prev (stash stride 5H) and x
-// (stride I) have 16-byte row strides.
-inline bool dw_on_tensor_cores(int I, int H) { return H % 4 == 0 && I % 4 == 0; }
-
 struct BwdLayout {
-  size_t dgi, dgh, wt, gemm, col, total;
-  int ldgi;  // row stride of dG_ih (multiple of 4 floats for TMA)
+  size_t dgi, dgh, wt, hp, xp, gemm, col, total;
+  int ldgi;      // row stride of dG_ih / dG_hh (multiple of 4 floats for TMA)
+  bool hp_copy;  // h_prev (stash stride 5H) needs a 16-byte-stride copy (H % 4 != 0)
+  bool x_copy;   // x (stride I) needs a 16-byte-stride copy (I % 4 != 0)
 };
 
 BwdLayout bwd_layout(int B, int T, int I, int H, int device) {
@@ -108,17 +106,19 @@ BwdLayout bwd_layout(int B, int T, int I, int H, int device) {
   off = align_up(off + sizeof(float) * BT * l.ldgi, kAlign);
   l.wt = off;
   off = align_up(off + sizeof(float) * (size_t)I * l.ldgi, kAlign);
+  l.hp_copy = H % 4 != 0;
+  l.x_copy = I % 4 != 0;
+  // Room for 16-byte-stride copies of h_prev and x, used when H or I is not a
+  // multiple of 4 or the caller's buffers are not 16-byte aligned.
+  l.hp = off;
+  off = align_up(off + sizeof(float) * BT * pad4(H), kAlign);
+  l.xp = off;
+  off = align_up(off + sizeof(float) * BT * pad4(I), kAlign);
   l.gemm = off;
-  // Weight-gradient products: tensor cores (split-K partials) when the
-  // operands have 16-byte row strides, else the exact FP64 SIMT contraction.
-  size_t g = 0;
-  if (dw_on_tensor_cores(I, H)) {
-    TcGemmArgs hh{nullptr, l.ldgi, nullptr, 5L * H, nullptr, H, nullptr, 3 * H, H, (int)BT, true, true};
-    TcGemmArgs ih{nullptr, l.ldgi, nullptr, I, nullptr, I, nullptr, 3 * H, I, (int)BT, true, true};
-    g = std::max(tc_gemm_ws_bytes(hh, device), tc_gemm_ws_bytes(ih, device));
-  } else {
-    g = std::max(gemm_ws_bytes(3 * H, H, (int)BT, device), gemm_ws_bytes(3 * H, I, (int)BT, device));
-  }
+  // Split-K partials of the weight-gradient products.
+  TcGemmArgs hh{nullptr, l.ldgi, nullptr, pad4(H), nullptr, H, nullptr, 3 * H, H, (int)BT, true, true};
+  TcGemmArgs ih{nullptr, l.ldgi, nullptr, pad4(I), nullptr, I, nullptr, 3 * H, I, (int)BT, true, true};
+  const size_t g = std::max(tc_gemm_ws_bytes(hh, device), tc_gemm_ws_bytes(ih, device));
   off = align_up(off + g, kAlign);
   l.col = off;
   off = align_up(off + bias_grad_ws_bytes(H), kAlign);
@@ -229,14 +229,10 @@ int gru_forward(const float* x, const float* h0, const float* w_ih, const float*
   // G = x . W_ih^T + b_ih on the tensor cores (3xTF32).
   TcGemmArgs ga{x, I, w_ih, I, G, 3 * H, b_ih, B * T, 3 * H, I};
   if (l.pad || !tc_gemm_supported(ga)) {
-    if (!l.pad) {
-      set_error("gru_forward: x and w_ih must be 16-byte aligned");
-      return GRU_ERR_INVALID;
-    }
     float* xp = reinterpret_cast<float*>(ws + l.xp);
     float* wp = reinterpret_cast<float*>(ws + l.wp);
-    if ((rc = pad_rows(x, (long)B * T, I, xp, pad4(I), stream))) return rc;
-    if ((rc = pad_rows(w_ih, 3L * H, I, wp, pad4(I), stream))) return rc;
+    if ((rc = pad_rows(x, (long)B * T, I, I, xp, pad4(I), stream))) return rc;
+    if ((rc = pad_rows(w_ih, 3L * H, I, I, wp, pad4(I), stream))) return rc;
     ga.A = xp;
     ga.lda = pad4(I);
     ga.B = wp;
@@ -294,23 +290,29 @@ int gru_backward(const float* dout, const float* dhn, const float* x, const floa
 
   const int BT = B * T;
   const int H3 = 3 * H;
-  // dW_hh = dG_hh^T . h_prev (h_prev = stash column block 4), dW_ih = dG_ih^T . x
-  if (dw_on_tensor_cores(I, H)) {
-    TcGemmArgs hh{dGh, l.ldgi, stash + 4 * H, 5L * H, dw_hh, H, nullptr, H3, H, BT, true, true};
-    TcGemmArgs ih{dGi, l.ldgi, x, I, dw_ih, I, nullptr, H3, I, BT, true, true};
-    if (tc_gemm_supported(hh) && tc_gemm_supported(ih)) {
-      if ((rc = tc_gemm(hh, stream, kKindGradGemm, gws, gws_bytes))) return rc;
-      if ((rc = tc_gemm(ih, stream, kKindGradGemm, gws, gws_bytes))) return rc;
-    } else {
-      set_error("gru_backward: x and stash must be 16-byte aligned");
-      return GRU_ERR_INVALID;
-    }
-  } else {
-    GemmArgs a1{dGh, 1, l.ldgi, stash + 4 * H, 5L * H, 1, dw_hh, H, nullptr, H3, H, BT};
-    if ((rc = gemm(a1, gws, gws_bytes, dev, stream, kKindGradGemm, true))) return rc;
-    GemmArgs a2{dGi, 1, l.ldgi, x, I, 1, dw_ih, I, nullptr, H3, I, BT};
-    if ((rc = gemm(a2, gws, gws_bytes, dev, stream, kKindGradGemm, true))) return rc;
+  // dW_hh = dG_hh^T . h_prev (h_prev = stash column block 4), dW_ih = dG_ih^T . x,
+  // on the tensor cores; operands without a 16-byte row stride are first
+  // copied into padded buffers.
+  const float* hp = stash + 4 * H;
+  long ldhp = 5L * H;
+  if (l.hp_copy || (reinterpret_cast<uintptr_t>(hp) & 15)) {
+    float* hpp = reinterpret_cast<float*>(ws + l.hp);
+    if ((rc = pad_rows(hp, BT, H, 5L * H, hpp, pad4(H), stream))) return rc;
+    hp = hpp;
+    ldhp = pad4(H);
   }
+  const float* xx = x;
+  long ldx = I;
+  if (l.x_copy || (reinterpret_cast<uintptr_t>(x) & 15)) {
+    float* xpp = reinterpret_cast<float*>(ws + l.xp);
+    if ((rc = pad_rows(x, BT, I, I, xpp, pad4(I), stream))) return rc;
+    xx = xpp;
+    ldx = pad4(I);
+  }
+  TcGemmArgs hh{dGh, l.ldgi, hp, ldhp, dw_hh, H, nullptr, H3, H, BT, true, true};
+  TcGemmArgs ih{dGi, l.ldgi, xx, ldx, dw_ih, I, nullptr, H3, I, BT, true, true};
+  if ((rc = tc_gemm(hh, stream, kKindGradGemm, gws, gws_bytes))) return rc;
+  if ((rc = tc_gemm(ih, stream, kKindGradGemm, gws, gws_bytes))) return rc;
   if (dx) {
     // dx = dG_ih . W_ih on the tensor cores, with W_ih^T staged as [I, ldgi].
     if ((rc = transpose(w_ih, H3, I, wt, l.ldgi, stream))) return rc;

@@ -65,24 +65,6 @@ int launch_rec_backward(const float* dout, const float* dhn, const float* w_hh,
                         const float* stash, float* dGi, int ldgi, float* dGh, float* dh0,
                         const RecGeom& g, cudaStream_t stream);
 
-// ---------------------------------------------------------------------------
-// Dense FP32-accurate contraction  C[m, n] = sum_k A(m, k) * B(k, n) (+ bias[n])
-// with A(m, k) = A[m*sam + k*sak] and B(k, n) = B[k*sbk + n*sbn] (one of each
-// pair of strides is 1).  `ws` provides split-K partials; gemm_ws_bytes() says
-// how many bytes a given shape needs.
-// ---------------------------------------------------------------------------
-struct GemmArgs {
-  const float* A; long sam, sak;
-  const float* B; long sbk, sbn;
-  float* C; long ldc;
-  const float* bias;  // [N] or null
-  int M, N, K;
-};
-size_t gemm_ws_bytes(int M, int N, int K, int device);
-// exact = true: FP64 products and accumulation (weight-gradient contractions).
-int gemm(const GemmArgs& a, void* ws, size_t ws_bytes, int device, cudaStream_t stream, int kind,
-         bool exact = false);
-
 // Tensor-core (tcgen05, 3xTF32) product C[m, n] = sum_k A(m, k) B(n, k) (+ bias).
 // K-major operand (a_mn = false): A [M, K] row-major, row stride lda.
 // MN-major operand (a_mn = true): A stored [K, M] row-major (K is the row),
@@ -103,9 +85,9 @@ size_t tc_gemm_ws_bytes(const TcGemmArgs& a, int device);
 int tc_gemm(const TcGemmArgs& a, cudaStream_t stream, int kind, void* ws = nullptr, size_t ws_bytes = 0);
 int read_gemm_status(int reset, int* status);
 
-// Small layout kernels: copy a [rows, cols] matrix into a row stride `ldd`
+// Small layout kernels: copy a [rows, cols] matrix of row stride lds into row stride `ldd`
 // (pad columns zeroed), and transpose [rows, cols] into [cols, ldd].
-int pad_rows(const float* src, long rows, int cols, float* dst, int ldd, cudaStream_t stream);
+int pad_rows(const float* src, long rows, int cols, long lds, float* dst, int ldd, cudaStream_t stream);
 int transpose(const float* src, int rows, int cols, float* dst, int ldd, cudaStream_t stream);
 
 // Bias gradients db_ih = colsum(dG_ih), db_hh = colsum(dG_hh) over `rows`
@@ -127,7 +109,7 @@ enum KernelKind {
   kKindInputGemm = 0,   // x . W_ih^T + b_ih
   kKindFwdRecurrent = 1,
   kKindBwdRecurrent = 2,
-  kKindGradGemm = 3,    // dW_hh, dW_ih, dx contractions (+ split-K reduce)
+  kKindGradGemm = 3,    // dW_hh, dW_ih, dx products (+ split-K reduce)
   kKindColsum = 4,      // db_ih / db_hh
   kKindLayout = 5,      // padding / transpose copies feeding the tensor-core products
   kKindCount = 6

@@ -1,7 +1,6 @@
-// FP32 strided contraction with deterministic split-K, and FP64-accumulated
-// column sums.  These implement the dense products around the GRU time loop:
-// the input projection x.W_ih^T + b_ih (prod/gru.py:519-523) and the gradient
-// contractions dW_hh, dx, dW_ih, db_* (prod/gru.py:569-578).
+// Bias gradients (FP64-accumulated column sums of dG, prod/gru.py:574/578)
+// and the small layout kernels (padding to 16-byte row strides, transpose)
+// that feed the tensor-core products.
 
 #include "common.cuh"
 #include "../../include/rnn_kernel_b200.h"
@@ -9,92 +8,6 @@
 namespace gru {
 
 namespace {
-
-constexpr int BM = 64, BN = 64, BK = 16;
-
-// C tile (or split-K partial) = A(m, k) B(k, n) over k in [k0, k1).
-// Acc = double: every FP32 x FP32 product is exact in FP64 and the sum is
-// accumulated in FP64 (used for the weight-gradient contractions whose K is
-// B*T); Acc = float: plain FP32 FMA (K = I or 3H).
-template <typename Acc>
-__global__ void __launch_bounds__(256)
-gemm_simt_kernel(GemmArgs a, int kchunk, Acc* partial) {
-  __shared__ float As[BK][BM + 4];
-  __shared__ float Bs[BK][BN + 4];
-  const int tid = threadIdx.x;
-  const int tx = tid & 15, ty = tid >> 4;
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-  const int k0 = blockIdx.z * kchunk;
-  const int k1 = min(a.K, k0 + kchunk);
-  Acc acc[4][4] = {};
-  const bool a_kfast = (a.sak == 1);
-  const bool b_nfast = (a.sbn == 1);
-  for (int kt = k0; kt < k1; kt += BK) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int e = tid + i * 256;
-      int mm, kk;
-      if (a_kfast) { mm = e / BK; kk = e % BK; }
-      else { kk = e / BM; mm = e % BM; }
-      const int m = m0 + mm, k = kt + kk;
-      As[kk][mm] = (m < a.M && k < k1) ? a.A[(long)m * a.sam + (long)k * a.sak] : 0.0f;
-      int nn, kb;
-      if (b_nfast) { kb = e / BN; nn = e % BN; }
-      else { nn = e / BK; kb = e % BK; }
-      const int n = n0 + nn, k2 = kt + kb;
-      Bs[kb][nn] = (n < a.N && k2 < k1) ? a.B[(long)k2 * a.sbk + (long)n * a.sbn] : 0.0f;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int kk = 0; kk < BK; ++kk) {
-      Acc av[4], bv[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) av[i] = As[kk][ty * 4 + i];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) bv[j] = Bs[kk][tx * 4 + j];
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fma(av[i], bv[j], acc[i][j]);
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int m = m0 + ty * 4 + i;
-    if (m >= a.M) continue;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int n = n0 + tx * 4 + j;
-      if (n >= a.N) continue;
-      if (partial != nullptr) {
-        partial[((size_t)blockIdx.z * a.M + m) * a.N + n] = acc[i][j];
-      } else {
-        a.C[(long)m * a.ldc + n] = (float)(acc[i][j] + (a.bias ? (Acc)a.bias[n] : (Acc)0));
-      }
-    }
-  }
-}
-
-template <typename Acc>
-__global__ void splitk_reduce_kernel(const Acc* partial, int S, GemmArgs a) {
-  const long MN = (long)a.M * a.N;
-  for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < MN; e += (long)gridDim.x * blockDim.x) {
-    double s = 0.0;
-    for (int z = 0; z < S; ++z) s += partial[z * MN + e];
-    const int m = (int)(e / a.N), n = (int)(e % a.N);
-    if (a.bias) s += a.bias[n];
-    a.C[(long)m * a.ldc + n] = (float)s;
-  }
-}
-
-int splits_for(int M, int N, int K, int device) {
-  const int tiles = ceil_div(M, BM) * ceil_div(N, BN);
-  const int sms = sm_count(device);
-  int S = 1;
-  while (tiles * S < 2 * sms && K / (S * 2) >= 256) S *= 2;
-  return S;
-}
 
 // Bias gradients.  dG_ih = [dr, dz, dn_pre] and dG_hh = [dr, dz, dhn] share
 // their r and z columns, so one pass sums the 3H columns of dG_ih and the n
@@ -132,12 +45,12 @@ __global__ void bias_grad_final_kernel(const double* __restrict__ part, int nchu
 
 constexpr int kColChunks = 256;
 
-__global__ void pad_rows_kernel(const float* src, long rows, int cols, float* dst, int ldd) {
+__global__ void pad_rows_kernel(const float* src, long rows, int cols, long lds, float* dst, int ldd) {
   const long n = rows * ldd;
   for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < n; e += (long)gridDim.x * blockDim.x) {
     const long r = e / ldd;
     const int c = (int)(e - r * ldd);
-    dst[e] = c < cols ? src[r * cols + c] : 0.0f;
+    dst[e] = c < cols ? src[r * lds + c] : 0.0f;
   }
 }
 
@@ -157,10 +70,10 @@ __global__ void transpose_kernel(const float* src, int rows, int cols, float* ds
 
 }  // namespace
 
-int pad_rows(const float* src, long rows, int cols, float* dst, int ldd, cudaStream_t stream) {
+int pad_rows(const float* src, long rows, int cols, long lds, float* dst, int ldd, cudaStream_t stream) {
   if (rows <= 0) return GRU_OK;
   LaunchScope scope(kKindLayout, stream);
-  pad_rows_kernel<<<1184, 256, 0, stream>>>(src, rows, cols, dst, ldd);
+  pad_rows_kernel<<<1184, 256, 0, stream>>>(src, rows, cols, lds, dst, ldd);
   GRU_CUDA_TRY(cudaGetLastError());
   return GRU_OK;
 }
@@ -172,41 +85,6 @@ int transpose(const float* src, int rows, int cols, float* dst, int ldd, cudaStr
   transpose_kernel<<<grid, dim3(32, 8), 0, stream>>>(src, rows, cols, dst, ldd);
   GRU_CUDA_TRY(cudaGetLastError());
   return GRU_OK;
-}
-
-size_t gemm_ws_bytes(int M, int N, int K, int device) {
-  const int S = splits_for(M, N, K, device);
-  return S > 1 ? sizeof(double) * (size_t)S * M * N : 0;
-}
-
-template <typename Acc>
-int gemm_impl(const GemmArgs& a, void* ws, size_t ws_bytes, int device, cudaStream_t stream, int kind) {
-  const int S = (a.K > 0 && ws != nullptr) ? splits_for(a.M, a.N, a.K, device) : 1;
-  const int kchunk = a.K > 0 ? ceil_div(ceil_div(a.K, S), BK) * BK : BK;
-  dim3 grid(ceil_div(a.N, BN), ceil_div(a.M, BM), S);
-  Acc* partial = nullptr;
-  if (S > 1) {
-    if (ws_bytes < gemm_ws_bytes(a.M, a.N, a.K, device)) {
-      set_error("gemm: workspace too small");
-      return GRU_ERR_INVALID;
-    }
-    partial = static_cast<Acc*>(ws);
-  }
-  LaunchScope scope(kind, stream, S > 1 ? 2 : 1);
-  gemm_simt_kernel<Acc><<<grid, 256, 0, stream>>>(a, kchunk, partial);
-  GRU_CUDA_TRY(cudaGetLastError());
-  if (S > 1) {
-    splitk_reduce_kernel<Acc><<<sm_count(device) * 4, 256, 0, stream>>>(partial, S, a);
-    GRU_CUDA_TRY(cudaGetLastError());
-  }
-  return GRU_OK;
-}
-
-int gemm(const GemmArgs& a, void* ws, size_t ws_bytes, int device, cudaStream_t stream, int kind,
-         bool exact) {
-  if (a.M <= 0 || a.N <= 0) return GRU_OK;
-  return exact ? gemm_impl<double>(a, ws, ws_bytes, device, stream, kind)
-               : gemm_impl<float>(a, ws, ws_bytes, device, stream, kind);
 }
 
 size_t bias_grad_ws_bytes(int H) { return sizeof(double) * (size_t)kColChunks * 4 * H; }

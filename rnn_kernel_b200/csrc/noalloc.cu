@@ -70,7 +70,7 @@ extern "C" int gru_forward_inference_noalloc(const float* x, const float* h0, co
   if (need > (size_t)GRU_NOALLOC_SCRATCH_BYTES) {
     set_error("gru_forward_inference_noalloc: this shape needs " + std::to_string(need) +
               " bytes of scratch, more than the static " + std::to_string((size_t)GRU_NOALLOC_SCRATCH_BYTES) +
-              " (B*T*3H*4 bytes must fit); use gru_forward with a caller workspace");
+              " (gru_forward_workspace_bytes(B, T, I, H) must fit); use gru_forward with a caller workspace");
     return GRU_ERR_UNSUPPORTED;
   }
   int dev = 0;
