@@ -66,60 +66,68 @@ int current_device(int* dev) {
 
 inline int pad4(int v) { return (v + 3) / 4 * 4; }
 
+// Workspace layouts.  The tensor-core products take pre-split operands
+// (hi = tf32(v), lo = tf32(v - hi)) with 16-byte row strides, so the
+// workspaces hold split copies of x, W_ih and h_prev, and the backward time
+// loop writes dG_ih / dG_hh already split.
 struct FwdLayout {
-  size_t g, xp, wp, total;
-  bool pad;  // x / W_ih need a copy with a 16-byte row stride for TMA
+  size_t g, xh, xl, wh, wl, total;
+  int ldx;  // row stride of the split x / W_ih copies (I rounded up to 4)
 };
 
 FwdLayout fwd_layout(int B, int T, int I, int H) {
   const long BT = (long)B * T;
   FwdLayout l{};
-  l.pad = (I % 4) != 0;
+  l.ldx = pad4(I);
   size_t off = 0;
   l.g = off;
   off = align_up(off + sizeof(float) * BT * 3 * H, kAlign);
-  // Room for 16-byte-stride copies of x and W_ih (I not a multiple of 4, or
-  // caller buffers not 16-byte aligned).
-  l.xp = off;
-  off = align_up(off + sizeof(float) * BT * pad4(I), kAlign);
-  l.wp = off;
-  off = align_up(off + sizeof(float) * (size_t)3 * H * pad4(I), kAlign);
+  l.xh = off;
+  off = align_up(off + sizeof(float) * BT * l.ldx, kAlign);
+  l.xl = off;
+  off = align_up(off + sizeof(float) * BT * l.ldx, kAlign);
+  l.wh = off;
+  off = align_up(off + sizeof(float) * (size_t)3 * H * l.ldx, kAlign);
+  l.wl = off;
+  off = align_up(off + sizeof(float) * (size_t)3 * H * l.ldx, kAlign);
   l.total = off;
   return l;
 }
 
 struct BwdLayout {
-  size_t dgi, dgh, wt, hp, xp, gemm, col, total;
-  int ldgi;      // row stride of dG_ih / dG_hh (multiple of 4 floats for TMA)
-  bool hp_copy;  // h_prev (stash stride 5H) needs a 16-byte-stride copy (H % 4 != 0)
-  bool x_copy;   // x (stride I) needs a 16-byte-stride copy (I % 4 != 0)
+  size_t dgih, dgil, dghh, dghl, wt, wth, wtl, hph, hpl, xh, xl, gemm, col, total;
+  int ldgi;  // row stride of dG_ih / dG_hh / W_ih^T (3H rounded up to 4)
+  int ldh;   // row stride of the split h_prev copy (H rounded up to 4)
+  int ldx;   // row stride of the split x copy (I rounded up to 4)
 };
 
 BwdLayout bwd_layout(int B, int T, int I, int H, int device) {
   const long BT = (long)B * T;
   BwdLayout l{};
   l.ldgi = pad4(3 * H);
+  l.ldh = pad4(H);
+  l.ldx = pad4(I);
   size_t off = 0;
-  l.dgi = off;
-  off = align_up(off + sizeof(float) * BT * l.ldgi, kAlign);
-  l.dgh = off;
-  off = align_up(off + sizeof(float) * BT * l.ldgi, kAlign);
-  l.wt = off;
-  off = align_up(off + sizeof(float) * (size_t)I * l.ldgi, kAlign);
-  l.hp_copy = H % 4 != 0;
-  l.x_copy = I % 4 != 0;
-  // Room for 16-byte-stride copies of h_prev and x, used when H or I is not a
-  // multiple of 4 or the caller's buffers are not 16-byte aligned.
-  l.hp = off;
-  off = align_up(off + sizeof(float) * BT * pad4(H), kAlign);
-  l.xp = off;
-  off = align_up(off + sizeof(float) * BT * pad4(I), kAlign);
-  l.gemm = off;
+  auto take = [&](size_t& at, size_t floats) {
+    at = off;
+    off = align_up(off + sizeof(float) * floats, kAlign);
+  };
+  take(l.dgih, (size_t)BT * l.ldgi);
+  take(l.dgil, (size_t)BT * l.ldgi);
+  take(l.dghh, (size_t)BT * l.ldgi);
+  take(l.dghl, (size_t)BT * l.ldgi);
+  take(l.wt, (size_t)I * l.ldgi);
+  take(l.wth, (size_t)I * l.ldgi);
+  take(l.wtl, (size_t)I * l.ldgi);
+  take(l.hph, (size_t)BT * l.ldh);
+  take(l.hpl, (size_t)BT * l.ldh);
+  take(l.xh, (size_t)BT * l.ldx);
+  take(l.xl, (size_t)BT * l.ldx);
   // Split-K partials of the weight-gradient products.
-  TcGemmArgs hh{nullptr, l.ldgi, nullptr, pad4(H), nullptr, H, nullptr, 3 * H, H, (int)BT, true, true};
-  TcGemmArgs ih{nullptr, l.ldgi, nullptr, pad4(I), nullptr, I, nullptr, 3 * H, I, (int)BT, true, true};
-  const size_t g = std::max(tc_gemm_ws_bytes(hh, device), tc_gemm_ws_bytes(ih, device));
-  off = align_up(off + g, kAlign);
+  TcGemmArgs hh{nullptr, l.ldgi, nullptr, l.ldh, nullptr, H, nullptr, 3 * H, H, (int)BT, true, true};
+  TcGemmArgs ih{nullptr, l.ldgi, nullptr, l.ldx, nullptr, I, nullptr, 3 * H, I, (int)BT, true, true};
+  l.gemm = off;
+  off = align_up(off + std::max(tc_gemm_ws_bytes(hh, device), tc_gemm_ws_bytes(ih, device)), kAlign);
   l.col = off;
   off = align_up(off + bias_grad_ws_bytes(H), kAlign);
   l.total = off;
@@ -226,18 +234,14 @@ int gru_forward(const float* x, const float* h0, const float* w_ih, const float*
   const FwdLayout l = fwd_layout(B, T, I, H);
   char* ws = static_cast<char*>(workspace);
   float* G = reinterpret_cast<float*>(ws + l.g);
-  // G = x . W_ih^T + b_ih on the tensor cores (3xTF32).
-  TcGemmArgs ga{x, I, w_ih, I, G, 3 * H, b_ih, B * T, 3 * H, I};
-  if (l.pad || !tc_gemm_supported(ga)) {
-    float* xp = reinterpret_cast<float*>(ws + l.xp);
-    float* wp = reinterpret_cast<float*>(ws + l.wp);
-    if ((rc = pad_rows(x, (long)B * T, I, I, xp, pad4(I), stream))) return rc;
-    if ((rc = pad_rows(w_ih, 3L * H, I, I, wp, pad4(I), stream))) return rc;
-    ga.A = xp;
-    ga.lda = pad4(I);
-    ga.B = wp;
-    ga.ldb = pad4(I);
-  }
+  float* xh = reinterpret_cast<float*>(ws + l.xh);
+  float* xl = reinterpret_cast<float*>(ws + l.xl);
+  float* wh = reinterpret_cast<float*>(ws + l.wh);
+  float* wl = reinterpret_cast<float*>(ws + l.wl);
+  // G = x . W_ih^T + b_ih on the tensor cores (3xTF32, pre-split operands).
+  if ((rc = split_tf32(x, (long)B * T, I, I, xh, xl, l.ldx, stream))) return rc;
+  if ((rc = split_tf32(w_ih, 3L * H, I, I, wh, wl, l.ldx, stream))) return rc;
+  TcGemmArgs ga{xh, l.ldx, wh, l.ldx, G, 3 * H, b_ih, B * T, 3 * H, I, false, false, xl, wl};
   if ((rc = tc_gemm(ga, stream, kKindInputGemm))) return rc;
   RecGeom g{};
   if ((rc = geometry(0, B, T, H, dev, &g))) return rc;
@@ -279,47 +283,35 @@ int gru_backward(const float* dout, const float* dhn, const float* x, const floa
     return GRU_ERR_INVALID;
   }
   char* ws = static_cast<char*>(workspace);
-  float* dGi = reinterpret_cast<float*>(ws + l.dgi);
-  float* dGh = reinterpret_cast<float*>(ws + l.dgh);
+  auto F = [&](size_t off) { return reinterpret_cast<float*>(ws + off); };
   void* gws = ws + l.gemm;
   const size_t gws_bytes = l.col - l.gemm;
-  float* wt = reinterpret_cast<float*>(ws + l.wt);
   RecGeom g{};
   if ((rc = geometry(1, B, T, H, dev, &g))) return rc;
-  if ((rc = launch_rec_backward(dout, dhn, w_hh, stash, dGi, l.ldgi, dGh, dh0, g, stream))) return rc;
+  if ((rc = launch_rec_backward(dout, dhn, w_hh, stash, F(l.dgih), F(l.dgil), l.ldgi, F(l.dghh), F(l.dghl), dh0,
+                                g, stream)))
+    return rc;
 
   const int BT = B * T;
   const int H3 = 3 * H;
-  // dW_hh = dG_hh^T . h_prev (h_prev = stash column block 4), dW_ih = dG_ih^T . x,
-  // on the tensor cores; operands without a 16-byte row stride are first
-  // copied into padded buffers.
-  const float* hp = stash + 4 * H;
-  long ldhp = 5L * H;
-  if (l.hp_copy || (reinterpret_cast<uintptr_t>(hp) & 15)) {
-    float* hpp = reinterpret_cast<float*>(ws + l.hp);
-    if ((rc = pad_rows(hp, BT, H, 5L * H, hpp, pad4(H), stream))) return rc;
-    hp = hpp;
-    ldhp = pad4(H);
-  }
-  const float* xx = x;
-  long ldx = I;
-  if (l.x_copy || (reinterpret_cast<uintptr_t>(x) & 15)) {
-    float* xpp = reinterpret_cast<float*>(ws + l.xp);
-    if ((rc = pad_rows(x, BT, I, I, xpp, pad4(I), stream))) return rc;
-    xx = xpp;
-    ldx = pad4(I);
-  }
-  TcGemmArgs hh{dGh, l.ldgi, hp, ldhp, dw_hh, H, nullptr, H3, H, BT, true, true};
-  TcGemmArgs ih{dGi, l.ldgi, xx, ldx, dw_ih, I, nullptr, H3, I, BT, true, true};
+  // dW_hh = dG_hh^T . h_prev (h_prev = stash column block 4), dW_ih = dG_ih^T . x
+  // on the tensor cores from pre-split copies.
+  if ((rc = split_tf32(stash + 4 * H, BT, H, 5L * H, F(l.hph), F(l.hpl), l.ldh, stream))) return rc;
+  if ((rc = split_tf32(x, BT, I, I, F(l.xh), F(l.xl), l.ldx, stream))) return rc;
+  TcGemmArgs hh{F(l.dghh), l.ldgi, F(l.hph), l.ldh, dw_hh, H, nullptr, H3, H, BT, true, true, F(l.dghl), F(l.hpl)};
+  TcGemmArgs ih{F(l.dgih), l.ldgi, F(l.xh), l.ldx, dw_ih, I, nullptr, H3, I, BT, true, true, F(l.dgil), F(l.xl)};
   if ((rc = tc_gemm(hh, stream, kKindGradGemm, gws, gws_bytes))) return rc;
   if ((rc = tc_gemm(ih, stream, kKindGradGemm, gws, gws_bytes))) return rc;
   if (dx) {
-    // dx = dG_ih . W_ih on the tensor cores, with W_ih^T staged as [I, ldgi].
-    if ((rc = transpose(w_ih, H3, I, wt, l.ldgi, stream))) return rc;
-    TcGemmArgs a3{dGi, l.ldgi, wt, l.ldgi, dx, I, nullptr, BT, I, H3};
+    // dx = dG_ih . W_ih, with W_ih^T staged (and split) as [I, ldgi].
+    if ((rc = transpose(w_ih, H3, I, F(l.wt), l.ldgi, stream))) return rc;
+    if ((rc = split_tf32(F(l.wt), I, l.ldgi, l.ldgi, F(l.wth), F(l.wtl), l.ldgi, stream))) return rc;
+    TcGemmArgs a3{F(l.dgih), l.ldgi, F(l.wth), l.ldgi, dx, I, nullptr, BT, I, H3, false, false, F(l.dgil), F(l.wtl)};
     if ((rc = tc_gemm(a3, stream, kKindGradGemm))) return rc;
   }
-  if ((rc = bias_grads(dGi, dGh, BT, H, l.ldgi, db_ih, db_hh, ws + l.col, stream))) return rc;
+  if ((rc = bias_grads(F(l.dgih), F(l.dgil), F(l.dghh), F(l.dghl), BT, H, l.ldgi, db_ih, db_hh, ws + l.col,
+                       stream)))
+    return rc;
   return GRU_OK;
 }
 

@@ -61,11 +61,15 @@ int rec_backward_geometry(int B, int T, int H, int device, RecGeom* g);
 int launch_rec_forward(const float* G, const float* h0, const float* w_hh, const float* b_hh,
                        float* out, float* hn, float* stash, const RecGeom& g,
                        cudaStream_t stream);
+// dG_ih / dG_hh are written pre-split (hi, lo) with row stride ldgi.
 int launch_rec_backward(const float* dout, const float* dhn, const float* w_hh,
-                        const float* stash, float* dGi, int ldgi, float* dGh, float* dh0,
+                        const float* stash, float* dGi, float* dGi_lo, int ldgi, float* dGh, float* dGh_lo,
+                        float* dh0,
                         const RecGeom& g, cudaStream_t stream);
 
 // Tensor-core (tcgen05, 3xTF32) product C[m, n] = sum_k A(m, k) B(n, k) (+ bias).
+// The operands come pre-split: A / A_lo hold tf32(a) and tf32(a - tf32(a))
+// (round to nearest) with the same layout, likewise B / B_lo.
 // K-major operand (a_mn = false): A [M, K] row-major, row stride lda.
 // MN-major operand (a_mn = true): A stored [K, M] row-major (K is the row),
 // row stride lda; same for B with N.  C [M, N], row stride ldc.  Operands
@@ -79,23 +83,27 @@ struct TcGemmArgs {
   const float* bias;
   int M, N, K;
   bool a_mn = false, b_mn = false;
+  const float* A_lo = nullptr;
+  const float* B_lo = nullptr;
 };
+// hi[r, c] = tf32(src[r, c]), lo[r, c] = tf32(src - hi) for c < cols, 0 for
+// cols <= c < ldd; src row stride lds, outputs row stride ldd.
+int split_tf32(const float* src, long rows, int cols, long lds, float* hi, float* lo, int ldd, cudaStream_t stream);
 bool tc_gemm_supported(const TcGemmArgs& a);
 size_t tc_gemm_ws_bytes(const TcGemmArgs& a, int device);
 int tc_gemm(const TcGemmArgs& a, cudaStream_t stream, int kind, void* ws = nullptr, size_t ws_bytes = 0);
 int read_gemm_status(int reset, int* status);
 
-// Small layout kernels: copy a [rows, cols] matrix of row stride lds into row stride `ldd`
-// (pad columns zeroed), and transpose [rows, cols] into [cols, ldd].
-int pad_rows(const float* src, long rows, int cols, long lds, float* dst, int ldd, cudaStream_t stream);
+// Transpose a [rows, cols] matrix into [cols, ldd] (columns rows .. ldd zeroed).
 int transpose(const float* src, int rows, int cols, float* dst, int ldd, cudaStream_t stream);
 
 // Bias gradients db_ih = colsum(dG_ih), db_hh = colsum(dG_hh) over `rows`
 // rows of row stride ld (FP64 accumulation, deterministic two-pass; the
 // shared r/z columns are summed once).  ws needs bias_grad_ws_bytes(H).
 size_t bias_grad_ws_bytes(int H);
-int bias_grads(const float* dgi, const float* dgh, long rows, int H, long ld, float* db_ih, float* db_hh, void* ws,
-               cudaStream_t stream);
+// dG given pre-split: the values summed are hi + lo.
+int bias_grads(const float* dgi, const float* dgi_lo, const float* dgh, const float* dgh_lo, long rows, int H,
+               long ld, float* db_ih, float* db_hh, void* ws, cudaStream_t stream);
 
 int sm_count(int device);
 

@@ -1,6 +1,5 @@
 // Bias gradients (FP64-accumulated column sums of dG, prod/gru.py:574/578)
-// and the small layout kernels (padding to 16-byte row strides, transpose)
-// that feed the tensor-core products.
+// and the W_ih transpose that feeds the dx product.
 
 #include "common.cuh"
 #include "../../include/rnn_kernel_b200.h"
@@ -13,21 +12,24 @@ namespace {
 // their r and z columns, so one pass sums the 3H columns of dG_ih and the n
 // block of dG_hh (virtual columns 3H .. 4H): db_ih = cols [0, 3H),
 // db_hh = [cols 0 .. 2H, cols 3H .. 4H).
-__global__ void bias_grad_partial_kernel(const float* __restrict__ dgi, const float* __restrict__ dgh, long rows,
+__global__ void bias_grad_partial_kernel(const float* __restrict__ dgi, const float* __restrict__ dgi_lo,
+                                         const float* __restrict__ dgh, const float* __restrict__ dgh_lo, long rows,
                                          int H, long ld, long rchunk, double* __restrict__ part) {
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
   if (col >= 4 * H) return;
-  const float* X = col < 3 * H ? dgi + col : dgh + (col - H);  // dG_hh n block = its columns 2H .. 3H
+  // dG_hh n block = its columns 2H .. 3H; values are hi + lo
+  const float* X = col < 3 * H ? dgi + col : dgh + (col - H);
+  const float* Y = col < 3 * H ? dgi_lo + col : dgh_lo + (col - H);
   const long r0 = blockIdx.y * rchunk, r1 = min(rows, r0 + rchunk);
   double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
   long r = r0;
-  for (; r + 4 <= r1; r += 4) {
+  for (; r + 2 <= r1; r += 2) {
     s0 += X[r * ld];
-    s1 += X[(r + 1) * ld];
-    s2 += X[(r + 2) * ld];
-    s3 += X[(r + 3) * ld];
+    s1 += Y[r * ld];
+    s2 += X[(r + 1) * ld];
+    s3 += Y[(r + 1) * ld];
   }
-  for (; r < r1; ++r) s0 += X[r * ld];
+  for (; r < r1; ++r) s0 += (double)X[r * ld] + (double)Y[r * ld];
   part[(long)blockIdx.y * 4 * H + col] = (s0 + s1) + (s2 + s3);
 }
 
@@ -45,15 +47,6 @@ __global__ void bias_grad_final_kernel(const double* __restrict__ part, int nchu
 
 constexpr int kColChunks = 256;
 
-__global__ void pad_rows_kernel(const float* src, long rows, int cols, long lds, float* dst, int ldd) {
-  const long n = rows * ldd;
-  for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < n; e += (long)gridDim.x * blockDim.x) {
-    const long r = e / ldd;
-    const int c = (int)(e - r * ldd);
-    dst[e] = c < cols ? src[r * lds + c] : 0.0f;
-  }
-}
-
 __global__ void transpose_kernel(const float* src, int rows, int cols, float* dst, int ldd) {
   __shared__ float tile[32][33];
   const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
@@ -70,14 +63,6 @@ __global__ void transpose_kernel(const float* src, int rows, int cols, float* ds
 
 }  // namespace
 
-int pad_rows(const float* src, long rows, int cols, long lds, float* dst, int ldd, cudaStream_t stream) {
-  if (rows <= 0) return GRU_OK;
-  LaunchScope scope(kKindLayout, stream);
-  pad_rows_kernel<<<1184, 256, 0, stream>>>(src, rows, cols, lds, dst, ldd);
-  GRU_CUDA_TRY(cudaGetLastError());
-  return GRU_OK;
-}
-
 int transpose(const float* src, int rows, int cols, float* dst, int ldd, cudaStream_t stream) {
   if (rows <= 0 || cols <= 0) return GRU_OK;
   LaunchScope scope(kKindLayout, stream);
@@ -89,14 +74,15 @@ int transpose(const float* src, int rows, int cols, float* dst, int ldd, cudaStr
 
 size_t bias_grad_ws_bytes(int H) { return sizeof(double) * (size_t)kColChunks * 4 * H; }
 
-int bias_grads(const float* dgi, const float* dgh, long rows, int H, long ld, float* db_ih, float* db_hh, void* ws,
-               cudaStream_t stream) {
+int bias_grads(const float* dgi, const float* dgi_lo, const float* dgh, const float* dgh_lo, long rows, int H,
+               long ld, float* db_ih, float* db_hh, void* ws, cudaStream_t stream) {
   if (H <= 0) return GRU_OK;
   const long rchunk = (rows + kColChunks - 1) / kColChunks;
   double* part = static_cast<double*>(ws);
   dim3 grid(ceil_div(4 * H, 128), kColChunks);
   LaunchScope scope(kKindColsum, stream, 2);
-  bias_grad_partial_kernel<<<grid, 128, 0, stream>>>(dgi, dgh, rows, H, ld, rchunk > 0 ? rchunk : 1, part);
+  bias_grad_partial_kernel<<<grid, 128, 0, stream>>>(dgi, dgi_lo, dgh, dgh_lo, rows, H, ld, rchunk > 0 ? rchunk : 1,
+                                                   part);
   GRU_CUDA_TRY(cudaGetLastError());
   bias_grad_final_kernel<<<ceil_div(4 * H, 128), 128, 0, stream>>>(part, kColChunks, H, db_ih, db_hh);
   GRU_CUDA_TRY(cudaGetLastError());

@@ -1,25 +1,24 @@
 // FP32-accurate dense products on the 5th-generation tensor cores (sm_100a).
 //
-//   C[m, n] = sum_k A[m, k] * B[n, k] (+ bias[n])      A: [M, K], B: [N, K], both K-major
+//   C[m, n] = sum_k A(m, k) * B(n, k) (+ bias[n])
 //
-// used for the input projection G = x . W_ih^T + b_ih (prod/gru.py:519-523)
-// and dx = dG_ih . W_ih (prod/gru.py:575).
+// used for the input projection G = x . W_ih^T + b_ih (prod/gru.py:519-523),
+// dx = dG_ih . W_ih (prod/gru.py:575) and the weight gradients
+// dW_hh = dG_hh^T . h_prev, dW_ih = dG_ih^T . x (prod/gru.py:569-576).
 //
-// Precision: "3xTF32".  Each FP32 operand a is split into a_hi = tf32(a) and
-// a_lo = tf32(a - a_hi) (round to nearest); the product is accumulated in FP32
-// in tensor memory as a_lo*b_hi + a_hi*b_lo + a_hi*b_hi, which keeps about 21
-// bits of every product -- FP32-level accuracy for the short K of these two
-// products (K = I or 3H).
+// Precision: "3xTF32".  Every FP32 operand a arrives pre-split into
+// a_hi = tf32(a) and a_lo = tf32(a - a_hi) (round to nearest; split_tf32()
+// or the producing kernel writes both), and the product is formed as
+// a_lo*b_hi + a_hi*b_lo + a_hi*b_hi, keeping about 21 bits of every product.
 //
-// Structure of one CTA (one 128 x BN output tile, 256 threads):
-//   warp 0      TMA producer: FP32 tiles of A and B (128-byte swizzle) into a
-//               `S`-deep shared-memory ring;
-//   warp 1      allocates the tensor-memory accumulator; lane 0 issues the
-//               tcgen05.mma instructions (3 per 8-wide K step) and commits
-//               each stage back to the producer;
-//   warps 2-7   split every landed stage in place into hi (rounded) + lo
-//               (separate buffer) and hand it to the MMA issuer;
-//   warps 4-7   epilogue: tcgen05.ld of the accumulator, + bias, stores.
+// Structure of one CTA (192 threads, persistent over output tiles):
+//   warp 0      TMA producer: the four tiles (A hi/lo, B hi/lo; 128-byte
+//               swizzle, unicast from this GPU's memory) of each K stage into
+//               an S-deep shared-memory ring;
+//   warp 1      allocates tensor memory; lane 0 issues the tcgen05.mma
+//               instructions (3 per 8-wide K step) and commits each stage;
+//   warps 2-5   drain every finished stage's accumulators into FP32 registers
+//               and store each finished tile.
 // Every mbarrier wait is bounded; on expiry the kernel records
 // GRU_STATUS_WAIT_TIMEOUT and winds down.
 
@@ -36,8 +35,7 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 32;           // fp32 elements per 128-byte swizzle row
-constexpr int kThreads = 256;
-constexpr int kTransformThreads = 192;  // warps 2..7
+constexpr int kThreads = 192;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -187,7 +185,8 @@ __device__ __forceinline__ Unit unit_of(int u, int tiles_n, int tiles, int M, in
 
 template <int BN, int S, int NPAIR, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
-gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ah, const __grid_constant__ CUtensorMap map_al,
+                   const __grid_constant__ CUtensorMap map_bh, const __grid_constant__ CUtensorMap map_bl,
                    float* __restrict__ C, long ldc, const float* __restrict__ bias, int M, int N, int K,
                    int kchunk, int splits) {
   using L = Smem<BN, S>;
@@ -196,9 +195,8 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bars = sbase + L::kBarOff;
-  // barriers: full[S], ready[S], empty[S], filled[NPAIR], drained[NPAIR]; then the TMEM slot
+  // barriers: full[S], (unused)[S], empty[S], filled[NPAIR], drained[NPAIR]; then the TMEM slot
   auto full = [&](int s) { return bars + 8u * s; };
-  auto ready = [&](int s) { return bars + 8u * (S + s); };
   auto empty = [&](int s) { return bars + 8u * (2 * S + s); };
   auto filled = [&](int p) { return bars + 8u * (3 * S + p); };
   auto drained = [&](int p) { return bars + 8u * (3 * S + NPAIR + p); };
@@ -213,7 +211,6 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full(s), 1);
-      mbar_init(ready(s), kTransformThreads);
       mbar_init(empty(s), 1);
     }
     for (int p = 0; p < NPAIR; ++p) {
@@ -223,8 +220,10 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0 && lane == 0) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_ah)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_al)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_bh)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_bl)) : "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -247,20 +246,28 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
           const int s = i % S;
           if (i >= S && !mbar_wait(empty(s), ((i / S) - 1) & 1)) { ok = false; break; }
           const uint32_t st = sbase + s * L::kStage;
-          mbar_arrive_expect_tx(full(s), L::kATile + L::kBTile);
+          mbar_arrive_expect_tx(full(s), 2 * (L::kATile + L::kBTile));
           const int k0 = w.kbeg + ks * kBK;
+          const uint32_t a_hi = st, a_lo = st + L::kATile, b_hi = st + 2 * L::kATile, b_lo = b_hi + L::kBTile;
           if (A_MN) {
 #pragma unroll
-            for (int j = 0; j < kBM / 32; ++j) tma_load_2d(st + j * 4096, &map_a, full(s), w.m0 + 32 * j, k0);
+            for (int j = 0; j < kBM / 32; ++j) {
+              tma_load_2d(a_hi + j * 4096, &map_ah, full(s), w.m0 + 32 * j, k0);
+              tma_load_2d(a_lo + j * 4096, &map_al, full(s), w.m0 + 32 * j, k0);
+            }
           } else {
-            tma_load_2d(st, &map_a, full(s), k0, w.m0);
+            tma_load_2d(a_hi, &map_ah, full(s), k0, w.m0);
+            tma_load_2d(a_lo, &map_al, full(s), k0, w.m0);
           }
           if (B_MN) {
 #pragma unroll
-            for (int j = 0; j < BN / 32; ++j)
-              tma_load_2d(st + 2 * L::kATile + j * 4096, &map_b, full(s), w.n0 + 32 * j, k0);
+            for (int j = 0; j < BN / 32; ++j) {
+              tma_load_2d(b_hi + j * 4096, &map_bh, full(s), w.n0 + 32 * j, k0);
+              tma_load_2d(b_lo + j * 4096, &map_bl, full(s), w.n0 + 32 * j, k0);
+            }
           } else {
-            tma_load_2d(st + 2 * L::kATile, &map_b, full(s), k0, w.n0);
+            tma_load_2d(b_hi, &map_bh, full(s), k0, w.n0);
+            tma_load_2d(b_lo, &map_bl, full(s), k0, w.n0);
           }
         }
       }
@@ -282,7 +289,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
         const Unit w = unit_of<BN>(u, tiles_n, tiles, M, K, kchunk);
         for (int ks = 0; ks < w.nk; ++ks, ++i) {
           const int s = i % S, p = i % NPAIR;
-          if (!mbar_wait(ready(s), (i / S) & 1)) { ok = false; break; }
+          if (!mbar_wait(full(s), (i / S) & 1)) { ok = false; break; }
           if (i >= NPAIR && !mbar_wait(drained(p), ((i / NPAIR) - 1) & 1)) { ok = false; break; }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           const uint32_t st = sbase + s * L::kStage;
@@ -302,123 +309,70 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_const
       }
     }
   } else {
-    // Warps 2..7 split each landed stage into hi (in place) + lo; warps 4..7
-    // also drain the accumulator pair of the previous stage into registers
-    // and store each finished tile.
-    const int tt = threadIdx.x - 64;
-    constexpr int kA4 = L::kATile / 16, kB4 = L::kBTile / 16;  // float4 count per tile
-    const bool drainer = warp >= 4;
+    // Warps 2..5 drain each finished stage's accumulator pair into FP32
+    // registers (lane quarter warp % 4 of tensor memory) and store each
+    // finished tile.
     const uint32_t taddr = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
     float acc[BN];
 #pragma unroll
     for (int c = 0; c < BN; ++c) acc[c] = 0.0f;
     bool ok = true;
-    int i = 0;       // stage being transformed
-    int d = 0;       // stage being drained
-    int du = blockIdx.x, dks = 0;  // unit and in-unit stage of stage d
-    Unit dw = unit_of<BN>(du, tiles_n, tiles, M, K, kchunk);
-    auto drain_one = [&]() -> bool {
-      // skip units without K work (they still produce a zero tile)
-      const int p = d % NPAIR;
-      if (!mbar_wait(filled(p), (d / NPAIR) & 1)) return false;
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-#pragma unroll
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        uint32_t rs[16], rb[16];
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-            : "=r"(rs[0]), "=r"(rs[1]), "=r"(rs[2]), "=r"(rs[3]), "=r"(rs[4]), "=r"(rs[5]), "=r"(rs[6]),
-              "=r"(rs[7]), "=r"(rs[8]), "=r"(rs[9]), "=r"(rs[10]), "=r"(rs[11]), "=r"(rs[12]), "=r"(rs[13]),
-              "=r"(rs[14]), "=r"(rs[15])
-            : "r"(taddr + (uint32_t)(BN * (2 * p + 1) + c0)));
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-            : "=r"(rb[0]), "=r"(rb[1]), "=r"(rb[2]), "=r"(rb[3]), "=r"(rb[4]), "=r"(rb[5]), "=r"(rb[6]),
-              "=r"(rb[7]), "=r"(rb[8]), "=r"(rb[9]), "=r"(rb[10]), "=r"(rb[11]), "=r"(rb[12]), "=r"(rb[13]),
-              "=r"(rb[14]), "=r"(rb[15])
-            : "r"(taddr + (uint32_t)(BN * (2 * p) + c0)));
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-        for (int jj = 0; jj < 16; ++jj) acc[c0 + jj] += __uint_as_float(rb[jj]) + __uint_as_float(rs[jj]);
-      }
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      mbar_arrive(drained(p));
-      ++d;
-      ++dks;
-      return true;
-    };
-    // Store the tile of unit dw (after its last stage is drained) and move on.
-    auto finish_units = [&]() {
-      while (du < units && dks >= dw.nk) {
-        const int row = dw.m0 + 32 * (warp & 3) + lane;
-        float* Cu = splits > 1 ? C + (long)dw.split * M * ldc : C;
-        const float* bu = splits > 1 ? nullptr : bias;
-        if (row < M) {
-          float* crow = Cu + (long)row * ldc + dw.n0;
-          const bool vec = (ldc % 4 == 0) && dw.n0 + BN <= N &&
-                           ((reinterpret_cast<uintptr_t>(crow) & 15) == 0);
-          if (vec) {
-#pragma unroll
-            for (int c = 0; c < BN; c += 4) {
-              float4 v = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
-              if (bu) {
-                v.x += bu[dw.n0 + c]; v.y += bu[dw.n0 + c + 1]; v.z += bu[dw.n0 + c + 2]; v.w += bu[dw.n0 + c + 3];
-              }
-              *reinterpret_cast<float4*>(crow + c) = v;
-            }
-          } else {
-#pragma unroll
-            for (int c = 0; c < BN; ++c) {
-              const int n = dw.n0 + c;
-              if (n < N) crow[c] = acc[c] + (bu ? bu[n] : 0.0f);
-            }
-          }
-        }
-#pragma unroll
-        for (int c = 0; c < BN; ++c) acc[c] = 0.0f;
-        du += gridDim.x;
-        dks = 0;
-        if (du < units) dw = unit_of<BN>(du, tiles_n, tiles, M, K, kchunk);
-      }
-    };
-    if (drainer) finish_units();
+    int d = 0;  // global stage counter of this CTA
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
       const Unit w = unit_of<BN>(u, tiles_n, tiles, M, K, kchunk);
-      for (int ks = 0; ks < w.nk; ++ks, ++i) {
-        const int s = i % S;
-        if (!mbar_wait(full(s), (i / S) & 1)) { ok = false; break; }
-        float4* a = reinterpret_cast<float4*>(smem + s * L::kStage);
-        float4* alo = a + kA4;
-        float4* b = alo + kA4;
-        float4* blo = b + kB4;
-        for (int e = tt; e < kA4 + kB4; e += kTransformThreads) {
-          float4* src = e < kA4 ? a + e : b + (e - kA4);
-          float4* dlo = e < kA4 ? alo + e : blo + (e - kA4);
-          const float4 v = *src;
-          uint4 hi, lo;
-          hi.x = to_tf32(v.x); hi.y = to_tf32(v.y); hi.z = to_tf32(v.z); hi.w = to_tf32(v.w);
-          lo.x = to_tf32(v.x - __uint_as_float(hi.x));
-          lo.y = to_tf32(v.y - __uint_as_float(hi.y));
-          lo.z = to_tf32(v.z - __uint_as_float(hi.z));
-          lo.w = to_tf32(v.w - __uint_as_float(hi.w));
-          *reinterpret_cast<uint4*>(src) = hi;
-          *reinterpret_cast<uint4*>(dlo) = lo;
+      for (int ks = 0; ks < w.nk; ++ks, ++d) {
+        const int p = d % NPAIR;
+        if (!mbar_wait(filled(p), (d / NPAIR) & 1)) { ok = false; break; }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          uint32_t rs[16], rb[16];
+          asm volatile(
+              "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+              : "=r"(rs[0]), "=r"(rs[1]), "=r"(rs[2]), "=r"(rs[3]), "=r"(rs[4]), "=r"(rs[5]), "=r"(rs[6]),
+                "=r"(rs[7]), "=r"(rs[8]), "=r"(rs[9]), "=r"(rs[10]), "=r"(rs[11]), "=r"(rs[12]), "=r"(rs[13]),
+                "=r"(rs[14]), "=r"(rs[15])
+              : "r"(taddr + (uint32_t)(BN * (2 * p + 1) + c0)));
+          asm volatile(
+              "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+              : "=r"(rb[0]), "=r"(rb[1]), "=r"(rb[2]), "=r"(rb[3]), "=r"(rb[4]), "=r"(rb[5]), "=r"(rb[6]),
+                "=r"(rb[7]), "=r"(rb[8]), "=r"(rb[9]), "=r"(rb[10]), "=r"(rb[11]), "=r"(rb[12]), "=r"(rb[13]),
+                "=r"(rb[14]), "=r"(rb[15])
+              : "r"(taddr + (uint32_t)(BN * (2 * p) + c0)));
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) acc[c0 + jj] += __uint_as_float(rb[jj]) + __uint_as_float(rs[jj]);
         }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mbar_arrive(ready(s));
-        // Drain the previous stage (the tensor cores are already on this one).
-        if (drainer && d < i) {
-          if (!drain_one()) { ok = false; break; }
-          finish_units();
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        mbar_arrive(drained(p));
+      }
+      if (!ok) break;
+      // tile finished (units without K work produce a zero tile)
+      const int row = w.m0 + 32 * (warp & 3) + lane;
+      float* Cu = splits > 1 ? C + (long)w.split * M * ldc : C;
+      const float* bu = splits > 1 ? nullptr : bias;
+      if (row < M) {
+        float* crow = Cu + (long)row * ldc + w.n0;
+        const bool vec = (ldc % 4 == 0) && w.n0 + BN <= N && ((reinterpret_cast<uintptr_t>(crow) & 15) == 0);
+        if (vec) {
+#pragma unroll
+          for (int c = 0; c < BN; c += 4) {
+            float4 v = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
+            if (bu) {
+              v.x += bu[w.n0 + c]; v.y += bu[w.n0 + c + 1]; v.z += bu[w.n0 + c + 2]; v.w += bu[w.n0 + c + 3];
+            }
+            *reinterpret_cast<float4*>(crow + c) = v;
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < BN; ++c) {
+            const int n = w.n0 + c;
+            if (n < N) crow[c] = acc[c] + (bu ? bu[n] : 0.0f);
+          }
         }
       }
-    }
-    if (drainer) {
-      while (ok && d < i) {
-        if (!drain_one()) { ok = false; break; }
-        finish_units();
-      }
-      if (ok) finish_units();
+#pragma unroll
+      for (int c = 0; c < BN; ++c) acc[c] = 0.0f;
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -500,21 +454,77 @@ int launch_tc(const TcGemmArgs& a, float* C, long ldc, const float* bias, int sp
     GRU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, LDefault::kBytes));
     configured_device = dev;
   }
-  CUtensorMap ma, mb;
-  int rc = A_MN ? make_map(&ma, a.A, a.K, a.M, a.lda, 32, kBK, true)
-                : make_map(&ma, a.A, a.M, a.K, a.lda, kBK, kBM, false);
-  if (rc) return rc;
-  rc = B_MN ? make_map(&mb, a.B, a.K, a.N, a.ldb, 32, kBK, true)
-            : make_map(&mb, a.B, a.N, a.K, a.ldb, kBK, kBN, false);
-  if (rc) return rc;
+  CUtensorMap mah, mal, mbh, mbl;
+  int rc;
+  if (A_MN) {
+    if ((rc = make_map(&mah, a.A, a.K, a.M, a.lda, 32, kBK, true))) return rc;
+    if ((rc = make_map(&mal, a.A_lo, a.K, a.M, a.lda, 32, kBK, true))) return rc;
+  } else {
+    if ((rc = make_map(&mah, a.A, a.M, a.K, a.lda, kBK, kBM, false))) return rc;
+    if ((rc = make_map(&mal, a.A_lo, a.M, a.K, a.lda, kBK, kBM, false))) return rc;
+  }
+  if (B_MN) {
+    if ((rc = make_map(&mbh, a.B, a.K, a.N, a.ldb, 32, kBK, true))) return rc;
+    if ((rc = make_map(&mbl, a.B_lo, a.K, a.N, a.ldb, 32, kBK, true))) return rc;
+  } else {
+    if ((rc = make_map(&mbh, a.B, a.N, a.K, a.ldb, kBK, kBN, false))) return rc;
+    if ((rc = make_map(&mbl, a.B_lo, a.N, a.K, a.ldb, kBK, kBN, false))) return rc;
+  }
   const int units = ((a.M + kBM - 1) / kBM) * ((a.N + kBN - 1) / kBN) * splits;
   const int grid = units < sm_count(dev) ? units : sm_count(dev);
-  kern<<<grid, kThreads, LDefault::kBytes, stream>>>(ma, mb, C, ldc, bias, a.M, a.N, a.K, kchunk, splits);
+  kern<<<grid, kThreads, LDefault::kBytes, stream>>>(mah, mal, mbh, mbl, C, ldc, bias, a.M, a.N, a.K, kchunk, splits);
   GRU_CUDA_TRY(cudaGetLastError());
   return GRU_OK;
 }
 
+__device__ __forceinline__ void split4(float4 v, float4& h, float4& l) {
+  h = make_float4(__uint_as_float(to_tf32(v.x)), __uint_as_float(to_tf32(v.y)), __uint_as_float(to_tf32(v.z)),
+                  __uint_as_float(to_tf32(v.w)));
+  l = make_float4(__uint_as_float(to_tf32(v.x - h.x)), __uint_as_float(to_tf32(v.y - h.y)),
+                  __uint_as_float(to_tf32(v.z - h.z)), __uint_as_float(to_tf32(v.w - h.w)));
+}
+
+// One row per (blockIdx.x + k * gridDim.x), threads across the columns;
+// float4 when the source rows allow it (vec), else scalar.
+__global__ void split_tf32_kernel(const float* __restrict__ src, long rows, int cols, long lds,
+                                  float* __restrict__ hi, float* __restrict__ lo, int ldd, bool vec) {
+  for (long r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float* sr = src + r * lds;
+    float* hr = hi + r * ldd;
+    float* lr = lo + r * ldd;
+    if (vec) {
+      for (int c = 4 * threadIdx.x; c < ldd; c += 4 * blockDim.x) {
+        const float4 v = c < cols ? *reinterpret_cast<const float4*>(sr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 h, l;
+        split4(v, h, l);
+        *reinterpret_cast<float4*>(hr + c) = h;
+        *reinterpret_cast<float4*>(lr + c) = l;
+      }
+    } else {
+      for (int c = threadIdx.x; c < ldd; c += blockDim.x) {
+        const float v = c < cols ? sr[c] : 0.0f;
+        const uint32_t h = to_tf32(v);
+        hr[c] = __uint_as_float(h);
+        lr[c] = __uint_as_float(to_tf32(v - __uint_as_float(h)));
+      }
+    }
+  }
+}
+
 }  // namespace
+
+int split_tf32(const float* src, long rows, int cols, long lds, float* hi, float* lo, int ldd, cudaStream_t stream) {
+  if (rows <= 0) return GRU_OK;
+  const bool vec = cols % 4 == 0 && lds % 4 == 0 && ldd % 4 == 0 &&
+                   ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(hi) |
+                     reinterpret_cast<uintptr_t>(lo)) & 15) == 0;
+  const int threads = ldd >= 1024 ? 256 : (ldd >= 256 ? 64 : 32);
+  const long blocks = rows < 16384 ? rows : 16384;
+  LaunchScope scope(kKindLayout, stream);
+  split_tf32_kernel<<<(unsigned)blocks, threads, 0, stream>>>(src, rows, cols, lds, hi, lo, ldd, vec);
+  GRU_CUDA_TRY(cudaGetLastError());
+  return GRU_OK;
+}
 
 int read_gemm_status(int reset, int* status) {
   GRU_CUDA_TRY(cudaMemcpyFromSymbol(status, g_gemm_status, sizeof(int)));
@@ -526,7 +536,8 @@ int read_gemm_status(int reset, int* status) {
 }
 
 bool tc_gemm_supported(const TcGemmArgs& a) {
-  return ((reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.B)) & 15) == 0 &&
+  if (!a.A_lo || !a.B_lo) return false;
+  return ((reinterpret_cast<uintptr_t>(a.A_lo) | reinterpret_cast<uintptr_t>(a.B_lo)) & 15) == 0 && ((reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.B)) & 15) == 0 &&
          a.lda % 4 == 0 && a.ldb % 4 == 0 && a.K >= 1;
 }
 
@@ -548,7 +559,7 @@ size_t tc_gemm_ws_bytes(const TcGemmArgs& a, int device) {
 int tc_gemm(const TcGemmArgs& a, cudaStream_t stream, int kind, void* ws, size_t ws_bytes) {
   if (a.M <= 0 || a.N <= 0) return GRU_OK;
   if (!tc_gemm_supported(a)) {
-    set_error("tc_gemm: operands must be 16-byte aligned with row strides a multiple of 4 floats");
+    set_error("tc_gemm: operands must be pre-split (hi and lo), 16-byte aligned, with row strides a multiple of 4 floats");
     return GRU_ERR_INVALID;
   }
   int dev = 0;

@@ -124,6 +124,16 @@ __device__ __forceinline__ void cp_async_wait_dyn(int n) {
 
 // 1/(1+e^-v): __frcp_rn is the correctly rounded reciprocal, i.e. bit-identical
 // to the IEEE division 1.0f / (1.0f + e) and cheaper.
+// Store v as the pair (tf32(v), tf32(v - tf32(v))), both round to nearest.
+__device__ __forceinline__ void split_store(float* hi, float* lo, float v) {
+  uint32_t h, l;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(v));
+  const float r = v - __uint_as_float(h);
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l) : "f"(r));
+  *hi = __uint_as_float(h);
+  *lo = __uint_as_float(l);
+}
+
 __device__ __forceinline__ float sigmoidf_acc(float v) { return __frcp_rn(1.0f + expf(-v)); }
 
 // Parity of the mbarrier phase that carries the data consumed at iteration
@@ -336,9 +346,13 @@ struct BwdArgs {
   const float* dhn;    // [B,H] or null
   const float* w_hh;   // [3H,H]
   const float* stash;  // [B,T,5H]
-  float* dGi;          // [B,T,3H] with row stride ldgi
+  // dG_ih / dG_hh [B,T,3H] (row stride ldgi), each written pre-split for the
+  // tensor-core products: hi = tf32(v), lo = tf32(v - hi).
+  float* dGi;
+  float* dGi_lo;
   int ldgi;
-  float* dGh;          // [B,T,3H] with row stride ldgi
+  float* dGh;
+  float* dGh_lo;
   float* dh0;          // [B,H]
 };
 
@@ -486,14 +500,13 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
         dgs[(s * 3 + 2) * 32 + jl] = dhn_gate;
         gz[b * Hc + jl] = gg * z;
         const size_t row = (size_t)(b_begin + b) * T + t;
-        float* gi = a.dGi + row * a.ldgi + j;
-        float* gh = a.dGh + row * a.ldgi + j;
-        gi[0] = dr_pre;
-        gi[H] = dz_pre;
-        gi[2 * H] = dn_pre;
-        gh[0] = dr_pre;
-        gh[H] = dz_pre;
-        gh[2 * H] = dhn_gate;
+        const size_t o = row * a.ldgi + j;
+        split_store(a.dGi + o, a.dGi_lo + o, dr_pre);
+        split_store(a.dGi + o + H, a.dGi_lo + o + H, dz_pre);
+        split_store(a.dGi + o + 2 * H, a.dGi_lo + o + 2 * H, dn_pre);
+        split_store(a.dGh + o, a.dGh_lo + o, dr_pre);
+        split_store(a.dGh + o + H, a.dGh_lo + o + H, dz_pre);
+        split_store(a.dGh + o + 2 * H, a.dGh_lo + o + 2 * H, dhn_gate);
       }
       __syncthreads();
       // Every thread has consumed slot `rslot`: re-arm it for iteration it+2
@@ -749,9 +762,9 @@ int launch_rec_forward(const float* G, const float* h0, const float* w_hh, const
 }
 
 int launch_rec_backward(const float* dout, const float* dhn, const float* w_hh,
-                        const float* stash, float* dGi, int ldgi, float* dGh, float* dh0,
-                        const RecGeom& g, cudaStream_t stream) {
-  BwdArgs a{dout, dhn, w_hh, stash, dGi, ldgi, dGh, dh0};
+                        const float* stash, float* dGi, float* dGi_lo, int ldgi, float* dGh, float* dGh_lo,
+                        float* dh0, const RecGeom& g, cudaStream_t stream) {
+  BwdArgs a{dout, dhn, w_hh, stash, dGi, dGi_lo, ldgi, dGh, dGh_lo, dh0};
   RecGeom gg = g;
   if ((reinterpret_cast<uintptr_t>(dout) | reinterpret_cast<uintptr_t>(stash)) & 15) gg.vec4 = 0;
   return launch_clusters(kernel_for(false, gg.R), a, gg, stream, kKindBwdRecurrent);
