@@ -679,6 +679,18 @@ int finish_geometry(RecGeom* g, int device, bool fwd, SmemFn smem_of) {
     bc = bc > kMaxRows ? bc - kMaxRows : bc - 1;
   }
   g->nclusters = ceil_div(g->B, g->bc);
+  if (g->nclusters > max_clusters) {
+    // More than one wave: the last wave would be part-empty while every wave
+    // costs as much as its widest cluster, so spread the rows evenly over
+    // whole waves (narrower clusters, each step cheaper).
+    const int waves = ceil_div(g->nclusters, max_clusters);
+    g->bc = ceil_div(g->B, waves * max_clusters);
+    g->R = g->bc < kMaxRows ? g->bc : kMaxRows;
+    g->bcp = ceil_div(g->bc, g->R) * g->R;
+    g->pd = 4;
+    while (g->pd > 2 && smem_of(*g) > (size_t)max_smem) --g->pd;
+    g->nclusters = ceil_div(g->B, g->bc);
+  }
   g->smem = smem_of(*g);
   if ((g->off1 | g->off2 | g->off3) & 3) {
     set_error("internal: recurrent shared-memory region not 16-byte aligned");

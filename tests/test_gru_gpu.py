@@ -85,6 +85,13 @@ def test_large_batch_many_clusters(B, T):
     assert_parity(mine, theirs, truth, weights="envelope")
 
 
+def test_large_batch_h256_two_waves():
+    # B=1100 at H=256 needs more clusters of 8 CTAs than are resident at once:
+    # the rows are spread evenly over two waves.
+    mine, theirs, truth = run_pair(16, 256, 1, 1100, 3, seed=1100)
+    assert_parity(mine, theirs, truth, weights="envelope")
+
+
 def test_hn_only_loss_grad_output_none():
     mine, theirs, truth = run_pair(6, 48, 2, 3, 7, seed=5, loss="hn_only")
     assert_parity(mine, theirs, truth)
