@@ -166,11 +166,13 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
   const int H = g.H, T = g.T, Hc = g.Hc, Kp = g.nw * 32, bcp = g.bcp, pd = g.pd;
   const int j0 = c * Hc;
   const int hcnt = max(1, min(Hc, H - j0));
+  // first pointwise item of this thread (row, unit) in a sub-chunk
+  const int my_s = tid / hcnt, my_jl = tid - my_s * hcnt;
 
   extern __shared__ __align__(16) float smem[];
   __shared__ __align__(8) unsigned long long mbar[2];
   float* hbuf = smem;                          // [2][bcp][Kp]
-  float* part = smem + g.off1;                 // [R][3][32 units][8 warp slots]
+  float* part = smem + g.off1;                 // [R][3][2 halves][32 units][4 warp slots]
   float* ring = smem + g.off2;                 // [pd][bcp][3][Hc]
   float* bsl = smem + g.off3;                  // [3][Hc] this CTA's slice of b_hh
   const int ring_stride = bcp * 3 * Hc;
@@ -276,18 +278,22 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
         }
       }
       // Partial of warp w for (row s, gate q, unit lane) goes to slot
-      // (w + lane/4) % 8 of that unit's 8-float row: conflict-free stores, and
-      // the pointwise thread reads the 8 partials with two float4 loads.
-      const int slot = (warp + (lane >> 2)) & 7;
+      // (w + lane/8) % 8 of that unit, stored as half slot/4, element slot%4:
+      // the 32 lanes hit 32 distinct banks, and the pointwise thread reads its
+      // unit's 8 partials with two float4 loads that are contiguous across
+      // lanes (4 wavefronts each).
+      const int slot = (warp + (lane >> 3)) & 7;
+      float* pw = part + ((slot >> 2) * 32 + lane) * 4 + (slot & 3);
 #pragma unroll
       for (int s = 0; s < R; ++s) {
 #pragma unroll
-        for (int q = 0; q < 3; ++q) part[((s * 3 + q) * 32 + lane) * 8 + slot] = acc[s][q].x + acc[s][q].y;
+        for (int q = 0; q < 3; ++q) pw[(s * 3 + q) * 256] = acc[s][q].x + acc[s][q].y;
       }
       if (b0 == 0) cp_async_wait_dyn(pd - 2);
       __syncthreads();
       // Every thread is past its wait on slot `cur`: re-arm it for step t+2.
-      if (b0 == 0 && tid == 0 && t + 2 < T) mbar_expect_tx(bar0 + 8 * cur, bytes_per_step);
+      // (the last thread: it has no pointwise item when R * hcnt < nthr)
+      if (b0 == 0 && tid == nthr - 1 && t + 2 < T) mbar_expect_tx(bar0 + 8 * cur, bytes_per_step);
 
       const int ns = min(R, nb - b0);
       // Threads without a pointwise item in the last sub-chunk issue the
@@ -298,10 +304,10 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
       const int nact = ns * hcnt;
       if (b0 + R >= nb && nact < nthr && tid >= nact && t + pd - 1 < T) issue(t + pd - 1, tid - nact, nthr - nact);
       for (int e = tid; e < ns * hcnt; e += nthr) {
-        const int s = e / hcnt, jl = e - s * hcnt;
+        const int s = e == tid ? my_s : e / hcnt, jl = e == tid ? my_jl : e - s * hcnt;
         const int b = b0 + s, j = j0 + jl;
-        const float4* pp = reinterpret_cast<const float4*>(part + ((s * 3) * 32 + jl) * 8);
-        const float4 r0 = pp[0], r1 = pp[1], z0 = pp[64], z1 = pp[65], n0 = pp[128], n1 = pp[129];
+        const float4* pp = reinterpret_cast<const float4*>(part + (s * 3) * 256 + jl * 4);
+        const float4 r0 = pp[0], r1 = pp[32], z0 = pp[64], z1 = pp[96], n0 = pp[128], n1 = pp[160];
         const float ar = bsl[jl] + (((r0.x + r0.y) + (r0.z + r0.w)) + ((r1.x + r1.y) + (r1.z + r1.w)));
         const float az = bsl[Hc + jl] + (((z0.x + z0.y) + (z0.z + z0.w)) + ((z1.x + z1.y) + (z1.z + z1.w)));
         const float an = bsl[2 * Hc + jl] + (((n0.x + n0.y) + (n0.z + n0.w)) + ((n1.x + n1.y) + (n1.z + n1.w)));
@@ -370,6 +376,8 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
   const int H = g.H, T = g.T, Hc = g.Hc, bcp = g.bcp, pd = g.pd, C = g.C;
   const int j0 = c * Hc;
   const int hcnt = max(1, min(Hc, H - j0));
+  // first pointwise item of this thread (row, unit) in a sub-chunk
+  const int my_s = tid / hcnt, my_jl = tid - my_s * hcnt;
   // GEMV mapping: lane l of warp w owns the W_hh columns k0 = 32w + 2(l & 15)
   // and k0 + 1 for the half jh = l >> 4 of this CTA's units (16 each).
   const int jh = lane >> 4;
@@ -472,7 +480,7 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
       const int nact = ns * hcnt;
       if (b0 + R >= nb && nact < nthr && tid >= nact && it + pd - 1 < T) issue(it + pd - 1, tid - nact, nthr - nact);
       for (int e = tid; e < ns * hcnt; e += nthr) {
-        const int s = e / hcnt, jl = e - s * hcnt;
+        const int s = e == tid ? my_s : e / hcnt, jl = e == tid ? my_jl : e - s * hcnt;
         const int b = b0 + s, j = j0 + jl;
         float dh;
         if (it == 0) {
