@@ -122,8 +122,6 @@ __device__ __forceinline__ void cp_async_wait_dyn(int n) {
   else cp_async_wait<0>();
 }
 
-// 1/(1+e^-v): __frcp_rn is the correctly rounded reciprocal, i.e. bit-identical
-// to the IEEE division 1.0f / (1.0f + e) and cheaper.
 // Store v as the pair (tf32(v), tf32(v - tf32(v))), both round to nearest.
 __device__ __forceinline__ void split_store(float* hi, float* lo, float v) {
   uint32_t h, l;
@@ -134,7 +132,19 @@ __device__ __forceinline__ void split_store(float* hi, float* lo, float v) {
   *lo = __uint_as_float(l);
 }
 
-__device__ __forceinline__ float sigmoidf_acc(float v) { return __frcp_rn(1.0f + expf(-v)); }
+// 1/(1+e^-v).  The reciprocal is the hardware approximation (rcp.approx,
+// at most 1 ulp off) refined by one Newton-Raphson step y += y (1 - d y),
+// which leaves it within about 1 ulp of the exact quotient at a fraction of
+// the latency of the correctly rounded reciprocal on the step's critical
+// path.  v is clamped so that d stays finite (d = inf would give 0 * inf in
+// the refinement); sigmoid(-80) = 1.8e-35 is already 0 at the tolerance of
+// any use.
+__device__ __forceinline__ float sigmoidf_acc(float v) {
+  const float d = 1.0f + expf(-fmaxf(v, -80.0f));
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(d));
+  return fmaf(y, fmaf(-d, y, 1.0f), y);
+}
 
 // Parity of the mbarrier phase that carries the data consumed at iteration
 // `it` (>= 1) from a buffer used every other iteration: one buffer is first
