@@ -149,6 +149,8 @@ __device__ __forceinline__ float sigmoidf_acc(float v) {
 // Parity of the mbarrier phase that carries the data consumed at iteration
 // `it` (>= 1) from a buffer used every other iteration: one buffer is first
 // consumed at it = 1, the other at it = 2, then each every second iteration.
+constexpr int kPlan = 4;  // most per-step prefetch copies a thread keeps planned in registers
+
 __device__ __forceinline__ uint32_t phase_parity(int it) { return (uint32_t)((((it + 1) >> 1) - 1) & 1); }
 
 struct FwdArgs {
@@ -254,6 +256,58 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
     if (s < T) issue(s, tid, nthr);
     cp_async_commit();
   }
+  // In the time loop the same threads issue the same copies every step (the
+  // threads idle in the last sub-chunk's pointwise, else all threads after
+  // the sends): plan them once, so that a step's prefetch is address adds and
+  // copies only (no index divisions competing for issue slots with the GEMV).
+  const int ns_last = nb - ((nb - 1) / R) * R;
+  const int nact_last = ns_last * hcnt;
+  const bool idle_issue = nact_last < nthr;
+  const int pfirst = idle_issue ? tid - nact_last : tid, pstride = idle_issue ? nthr - nact_last : nthr;
+  int plan_n = 0;
+  int plan_dst[kPlan];
+  const float* plan_src[kPlan];
+  {
+    const int w = vec4 ? 4 : 1;
+    const int hw = hcnt / w, n = nb * 3 * hw;
+    const float* src0 = a.G + (size_t)b_begin * T * 3 * H + j0;
+#pragma unroll
+    for (int k = 0; k < kPlan; ++k) {
+      plan_dst[k] = 0;
+      plan_src[k] = src0;
+    }
+    if (pfirst >= 0 && pfirst + kPlan * pstride < n) plan_n = -1;  // more than kPlan copies: no plan
+    if (pfirst >= 0 && plan_n == 0) {
+#pragma unroll
+      for (int k = 0; k < kPlan; ++k) {
+        const int e = pfirst + k * pstride;
+        if (e < n) {
+          const int r = e / hw, jl = w * (e - r * hw);
+          const int b = r / 3, gi = r - 3 * b;
+          plan_dst[k] = r * Hc + jl;
+          plan_src[k] = src0 + (size_t)b * T * 3 * H + gi * H + jl;
+          plan_n = k + 1;
+        }
+      }
+    }
+  }
+  auto issue_step = [&](int s) {
+    if (plan_n < 0) {
+      issue(s, pfirst, pstride);
+      return;
+    }
+    float* dst = ring + (s % pd) * ring_stride;
+    const size_t so = (size_t)s * 3 * H;
+#pragma unroll
+    for (int k = 0; k < kPlan; ++k) {
+      if (k < plan_n) {
+        if (vec4)
+          cp_async16(dst + plan_dst[k], plan_src[k] + so);
+        else
+          cp_async4(dst + plan_dst[k], plan_src[k] + so);
+      }
+    }
+  };
 
   const uint32_t hbuf_u32 = smem_u32(hbuf);
   cluster.sync();  // buffers and mbarriers of every CTA initialised
@@ -312,7 +366,7 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
       // sent its step t-1 values, each of which depended on its reads of that
       // slot).
       const int nact = ns * hcnt;
-      if (b0 + R >= nb && nact < nthr && tid >= nact && t + pd - 1 < T) issue(t + pd - 1, tid - nact, nthr - nact);
+      if (b0 + R >= nb && idle_issue && tid >= nact && t + pd - 1 < T) issue_step(t + pd - 1);
       for (int e = tid; e < ns * hcnt; e += nthr) {
         const int s = e == tid ? my_s : e / hcnt, jl = e == tid ? my_jl : e - s * hcnt;
         const int b = b0 + s, j = j0 + jl;
@@ -347,10 +401,7 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
       if (b0 + R < nb) __syncthreads();  // `part` is reused by the next sub-chunk
     }
     // Every thread had a pointwise item: prefetch now, after the sends.
-    {
-      const int ns_last = nb - ((nb - 1) / R) * R;
-      if (ns_last * hcnt >= nthr && t + pd - 1 < T) issue(t + pd - 1, tid, nthr);
-    }
+    if (!idle_issue && t + pd - 1 < T) issue_step(t + pd - 1);
     cp_async_commit();
   }
   cp_async_wait<0>();
@@ -459,6 +510,60 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
     if (it < T) issue(it, tid, nthr);
     cp_async_commit();
   }
+  // Per-thread plan of the time loop's prefetch copies (as in the forward).
+  // Source of a copy at time s: plan_src + s * plan_ss (H for dout, 5H for
+  // the stash).
+  const int ns_last = nb - ((nb - 1) / R) * R;
+  const int nact_last = ns_last * hcnt;
+  const bool idle_issue = nact_last < nthr;
+  const int pfirst = idle_issue ? tid - nact_last : tid, pstride = idle_issue ? nthr - nact_last : nthr;
+  int plan_n = 0;
+  int plan_dst[kPlan], plan_ss[kPlan];
+  const float* plan_src[kPlan];
+  {
+    const int w = vec4 ? 4 : 1;
+    const int hw = hcnt / w, n = nb * 6 * hw;
+#pragma unroll
+    for (int k = 0; k < kPlan; ++k) {
+      plan_dst[k] = 0;
+      plan_ss[k] = 0;
+      plan_src[k] = a.stash;
+    }
+    if (a.dout == nullptr || (pfirst >= 0 && pfirst + kPlan * pstride < n)) plan_n = -1;
+    if (pfirst >= 0 && plan_n == 0) {
+#pragma unroll
+      for (int k = 0; k < kPlan; ++k) {
+        const int e = pfirst + k * pstride;
+        if (e < n) {
+          const int r = e / hw, jl = w * (e - r * hw);
+          const int b = r / 6, q = r - 6 * b;
+          const size_t row0 = (size_t)(b_begin + b) * T;
+          plan_dst[k] = r * Hc + jl;
+          plan_src[k] = q == 0 ? a.dout + row0 * H + j0 + jl : a.stash + row0 * 5 * H + (q - 1) * H + j0 + jl;
+          plan_ss[k] = q == 0 ? H : 5 * H;
+          plan_n = k + 1;
+        }
+      }
+    }
+  }
+  auto issue_step = [&](int it) {
+    if (plan_n < 0) {
+      issue(it, pfirst, pstride);
+      return;
+    }
+    const int s = T - 1 - it;
+    float* dst = ring + (it % pd) * ring_stride;
+#pragma unroll
+    for (int k = 0; k < kPlan; ++k) {
+      if (k < plan_n) {
+        const float* src = plan_src[k] + (size_t)s * plan_ss[k];
+        if (vec4)
+          cp_async16(dst + plan_dst[k], src);
+        else
+          cp_async4(dst + plan_dst[k], src);
+      }
+    }
+  };
 
   const int kown = (ksend < H) ? ksend / Hc : 0;
   const int kl = (ksend < H) ? ksend - kown * Hc : 0;
@@ -488,7 +593,7 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
       // (it-1) % pd: past this iteration's wait every CTA has sent its
       // iteration it-1 partials, which follow (barrier) its reads of the slot).
       const int nact = ns * hcnt;
-      if (b0 + R >= nb && nact < nthr && tid >= nact && it + pd - 1 < T) issue(it + pd - 1, tid - nact, nthr - nact);
+      if (b0 + R >= nb && idle_issue && tid >= nact && it + pd - 1 < T) issue_step(it + pd - 1);
       for (int e = tid; e < ns * hcnt; e += nthr) {
         const int s = e == tid ? my_s : e / hcnt, jl = e == tid ? my_jl : e - s * hcnt;
         const int b = b0 + s, j = j0 + jl;
@@ -574,10 +679,7 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
       }
     }
     // Every thread had a pointwise item: prefetch now, after the sends.
-    {
-      const int ns_last = nb - ((nb - 1) / R) * R;
-      if (ns_last * hcnt >= nthr && it + pd - 1 < T) issue(it + pd - 1, tid, nthr);
-    }
+    if (!idle_issue && it + pd - 1 < T) issue_step(it + pd - 1);
     cp_async_commit();
   }
 
