@@ -82,7 +82,7 @@ __device__ __forceinline__ unsigned long long global_ns() {
 }
 // Bounded wait: false (and the timeout recorded) if the phase did not
 // complete within kWaitLimitNs.
-__device__ __noinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
                                                unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
@@ -116,7 +116,10 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_dyn(int n) {
-  if (n >= 3) cp_async_wait<3>();
+  if (n >= 6) cp_async_wait<6>();
+  else if (n == 5) cp_async_wait<5>();
+  else if (n == 4) cp_async_wait<4>();
+  else if (n == 3) cp_async_wait<3>();
   else if (n == 2) cp_async_wait<2>();
   else if (n == 1) cp_async_wait<1>();
   else cp_async_wait<0>();
@@ -149,6 +152,7 @@ __device__ __forceinline__ float sigmoidf_acc(float v) {
 // Parity of the mbarrier phase that carries the data consumed at iteration
 // `it` (>= 1) from a buffer used every other iteration: one buffer is first
 // consumed at it = 1, the other at it = 2, then each every second iteration.
+constexpr int kMaxPrefetch = 8;  // deepest per-step input ring (steps)
 constexpr int kPlan = 4;  // most per-step prefetch copies a thread keeps planned in registers
 
 __device__ __forceinline__ uint32_t phase_parity(int it) { return (uint32_t)((((it + 1) >> 1) - 1) & 1); }
@@ -580,12 +584,14 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
     const int rslot = (it + 1) & 1;  // partials written at iteration it-1
     const float* rin = red + rslot * red_slot;
     const int wslot = it & 1;
+    // This thread's ring copies for iteration it (visible to all after the
+    // barrier below); waited for before the partials, whose wait absorbs it.
+    cp_async_wait_dyn(pd - 2);
     // After an expired wait (recorded in the status word) this thread stops
     // waiting but still runs every remaining barrier; results are then invalid.
     if (it > 0 && ok) ok = mbar_wait_bounded(bar0 + 8 * rslot, phase_parity(it));
 
     for (int b0 = 0; b0 < nb; b0 += R) {
-      if (b0 == 0) cp_async_wait_dyn(pd - 2);
       __syncthreads();
       const int ns = min(R, nb - b0);
       // Threads without a pointwise item in the last sub-chunk issue the
@@ -789,7 +795,7 @@ int finish_geometry(RecGeom* g, int device, bool fwd, SmemFn smem_of) {
     g->bc = bc;
     g->R = bc < kMaxRows ? bc : kMaxRows;
     g->bcp = ceil_div(bc, g->R) * g->R;
-    g->pd = 4;  // prefetch issued at the end of step t for step t + pd - 1
+    g->pd = kMaxPrefetch;  // prefetch issued at the end of step t for step t + pd - 1
     while (g->pd > 2 && smem_of(*g) > (size_t)max_smem) --g->pd;
     if (smem_of(*g) <= (size_t)max_smem) break;
     if (bc <= 1) {
@@ -807,7 +813,7 @@ int finish_geometry(RecGeom* g, int device, bool fwd, SmemFn smem_of) {
     g->bc = ceil_div(g->B, waves * max_clusters);
     g->R = g->bc < kMaxRows ? g->bc : kMaxRows;
     g->bcp = ceil_div(g->bc, g->R) * g->R;
-    g->pd = 4;
+    g->pd = kMaxPrefetch;
     while (g->pd > 2 && smem_of(*g) > (size_t)max_smem) --g->pd;
     g->nclusters = ceil_div(g->B, g->bc);
   }
