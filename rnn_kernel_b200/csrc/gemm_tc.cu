@@ -11,14 +11,16 @@
 // or the producing kernel writes both), and the product is formed as
 // a_lo*b_hi + a_hi*b_lo + a_hi*b_hi, keeping about 21 bits of every product.
 //
-// Structure of one CTA (192 threads, persistent over output tiles):
+// Structure of one CTA (320 threads, persistent over output tiles):
 //   warp 0      TMA producer: the four tiles (A hi/lo, B hi/lo; 128-byte
 //               swizzle, unicast from this GPU's memory) of each K stage into
 //               an S-deep shared-memory ring;
 //   warp 1      allocates tensor memory; lane 0 issues the tcgen05.mma
 //               instructions (3 per 8-wide K step) and commits each stage;
-//   warps 2-5   drain every finished stage's accumulators into FP32 registers
-//               and store each finished tile.
+//   warps 2-9   drain every finished stage's accumulators into FP32 registers
+//               (warp w: tensor-memory lane quarter w % 4, column half
+//               (w - 2) / 4; two 32-column load batches per stage) and store
+//               each finished tile.
 // Every mbarrier wait is bounded; on expiry the kernel records
 // GRU_STATUS_WAIT_TIMEOUT and winds down.
 
@@ -35,7 +37,8 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 32;           // fp32 elements per 128-byte swizzle row
-constexpr int kThreads = 192;
+constexpr int kDrainWarps = 8;    // 2 per tensor-memory lane quarter
+constexpr int kThreads = 64 + 32 * kDrainWarps;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -183,6 +186,20 @@ __device__ __forceinline__ Unit unit_of(int u, int tiles_n, int tiles, int M, in
   return w;
 }
 
+// 32 consecutive tensor-memory columns of this warp's lane quarter (one
+// 32-bit value per lane and column) into r[0..31]; completes at the next
+// tcgen05.wait::ld.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
 template <int BN, int S, int NPAIR, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ah, const __grid_constant__ CUtensorMap map_al,
@@ -215,7 +232,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ah, const __grid_cons
     }
     for (int p = 0; p < NPAIR; ++p) {
       mbar_init(filled(p), 1);
-      mbar_init(drained(p), 128);
+      mbar_init(drained(p), 32 * kDrainWarps);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -309,13 +326,16 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ah, const __grid_cons
       }
     }
   } else {
-    // Warps 2..5 drain each finished stage's accumulator pair into FP32
-    // registers (lane quarter warp % 4 of tensor memory) and store each
-    // finished tile.
-    const uint32_t taddr = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
-    float acc[BN];
+    // Warps 2..9 drain each finished stage's accumulator pair into FP32
+    // registers: warp w reads tensor-memory lanes 32 (w % 4) .. +31 (the only
+    // quarter it may access) and the column half (w - 2) / 4, and stores that
+    // part of each finished tile.
+    constexpr int kCW = BN / 2;  // columns per drain warp
+    const int quarter = warp & 3, chalf = (warp - 2) >> 2;
+    const uint32_t taddr = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(kCW * chalf);
+    float acc[kCW];
 #pragma unroll
-    for (int c = 0; c < BN; ++c) acc[c] = 0.0f;
+    for (int c = 0; c < kCW; ++c) acc[c] = 0.0f;
     bool ok = true;
     int d = 0;  // global stage counter of this CTA
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
@@ -325,54 +345,45 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ah, const __grid_cons
         if (!mbar_wait(filled(p), (d / NPAIR) & 1)) { ok = false; break; }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-          uint32_t rs[16], rb[16];
-          asm volatile(
-              "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-              : "=r"(rs[0]), "=r"(rs[1]), "=r"(rs[2]), "=r"(rs[3]), "=r"(rs[4]), "=r"(rs[5]), "=r"(rs[6]),
-                "=r"(rs[7]), "=r"(rs[8]), "=r"(rs[9]), "=r"(rs[10]), "=r"(rs[11]), "=r"(rs[12]), "=r"(rs[13]),
-                "=r"(rs[14]), "=r"(rs[15])
-              : "r"(taddr + (uint32_t)(BN * (2 * p + 1) + c0)));
-          asm volatile(
-              "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-              : "=r"(rb[0]), "=r"(rb[1]), "=r"(rb[2]), "=r"(rb[3]), "=r"(rb[4]), "=r"(rb[5]), "=r"(rb[6]),
-                "=r"(rb[7]), "=r"(rb[8]), "=r"(rb[9]), "=r"(rb[10]), "=r"(rb[11]), "=r"(rb[12]), "=r"(rb[13]),
-                "=r"(rb[14]), "=r"(rb[15])
-              : "r"(taddr + (uint32_t)(BN * (2 * p) + c0)));
+        for (int c0 = 0; c0 < kCW; c0 += 32) {
+          uint32_t rs[32], rb[32];
+          tmem_ld32(taddr + (uint32_t)(BN * (2 * p + 1) + c0), rs);
+          tmem_ld32(taddr + (uint32_t)(BN * (2 * p) + c0), rb);
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) acc[c0 + jj] += __uint_as_float(rb[jj]) + __uint_as_float(rs[jj]);
+          for (int jj = 0; jj < 32; ++jj) acc[c0 + jj] += __uint_as_float(rb[jj]) + __uint_as_float(rs[jj]);
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         mbar_arrive(drained(p));
       }
       if (!ok) break;
       // tile finished (units without K work produce a zero tile)
-      const int row = w.m0 + 32 * (warp & 3) + lane;
+      const int row = w.m0 + 32 * quarter + lane;
+      const int n0 = w.n0 + kCW * chalf;
       float* Cu = splits > 1 ? C + (long)w.split * M * ldc : C;
       const float* bu = splits > 1 ? nullptr : bias;
       if (row < M) {
-        float* crow = Cu + (long)row * ldc + w.n0;
-        const bool vec = (ldc % 4 == 0) && w.n0 + BN <= N && ((reinterpret_cast<uintptr_t>(crow) & 15) == 0);
+        float* crow = Cu + (long)row * ldc + n0;
+        const bool vec = (ldc % 4 == 0) && n0 + kCW <= N && ((reinterpret_cast<uintptr_t>(crow) & 15) == 0);
         if (vec) {
 #pragma unroll
-          for (int c = 0; c < BN; c += 4) {
+          for (int c = 0; c < kCW; c += 4) {
             float4 v = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
             if (bu) {
-              v.x += bu[w.n0 + c]; v.y += bu[w.n0 + c + 1]; v.z += bu[w.n0 + c + 2]; v.w += bu[w.n0 + c + 3];
+              v.x += bu[n0 + c]; v.y += bu[n0 + c + 1]; v.z += bu[n0 + c + 2]; v.w += bu[n0 + c + 3];
             }
             *reinterpret_cast<float4*>(crow + c) = v;
           }
         } else {
 #pragma unroll
-          for (int c = 0; c < BN; ++c) {
-            const int n = w.n0 + c;
+          for (int c = 0; c < kCW; ++c) {
+            const int n = n0 + c;
             if (n < N) crow[c] = acc[c] + (bu ? bu[n] : 0.0f);
           }
         }
       }
 #pragma unroll
-      for (int c = 0; c < BN; ++c) acc[c] = 0.0f;
+      for (int c = 0; c < kCW; ++c) acc[c] = 0.0f;
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
