@@ -153,7 +153,9 @@ __device__ __forceinline__ float sigmoidf_acc(float v) {
 // `it` (>= 1) from a buffer used every other iteration: one buffer is first
 // consumed at it = 1, the other at it = 2, then each every second iteration.
 constexpr int kMaxPrefetch = 8;  // deepest per-step input ring (steps)
-constexpr int kPlan = 4;  // most per-step prefetch copies a thread keeps planned in registers
+// most per-step prefetch items (a row's inputs for 1 or 4 units) a thread
+// keeps planned in registers
+constexpr int kPlanItems = 2;
 
 __device__ __forceinline__ uint32_t phase_parity(int it) { return (uint32_t)((((it + 1) >> 1) - 1) & 1); }
 
@@ -268,28 +270,32 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
   const int nact_last = ns_last * hcnt;
   const bool idle_issue = nact_last < nthr;
   const int pfirst = idle_issue ? tid - nact_last : tid, pstride = idle_issue ? nthr - nact_last : nthr;
-  int plan_n = 0;
-  int plan_dst[kPlan];
-  const float* plan_src[kPlan];
+  // Entry k of the plan: gates gi0 .. gi0 + cpe - 1 of row b, units
+  // jl .. jl + w - 1 of this CTA, to ring offsets plan_dst[k] + gi * Hc from
+  // G_c + s * 3H + plan_off[k] + gi * H (G_c = this cluster's rows, this CTA's
+  // units).  cpe (copies per entry, 1 or 3) is the smallest that keeps every
+  // thread at kPlanItems entries or fewer.
+  int plan_n = 0, cpe = 1;
+  int plan_dst[kPlanItems], plan_off[kPlanItems];
+  const float* const G_c = a.G + (size_t)b_begin * T * 3 * H + j0;
   {
     const int w = vec4 ? 4 : 1;
-    const int hw = hcnt / w, n = nb * 3 * hw;
-    const float* src0 = a.G + (size_t)b_begin * T * 3 * H + j0;
+    const int hw = hcnt / w;
 #pragma unroll
-    for (int k = 0; k < kPlan; ++k) {
-      plan_dst[k] = 0;
-      plan_src[k] = src0;
-    }
-    if (pfirst >= 0 && pfirst + kPlan * pstride < n) plan_n = -1;  // more than kPlan copies: no plan
+    for (int k = 0; k < kPlanItems; ++k) plan_dst[k] = plan_off[k] = 0;
+    if (pstride > 0 && nb * 3 * hw > kPlanItems * pstride) cpe = 3;
+    const int n = nb * (3 / cpe) * hw;
+    // more than kPlanItems entries, or offsets beyond 32 bits: no plan
+    if ((pfirst >= 0 && pfirst + kPlanItems * pstride < n) || (size_t)nb * T * 3 * H >= (1ull << 31)) plan_n = -1;
     if (pfirst >= 0 && plan_n == 0) {
 #pragma unroll
-      for (int k = 0; k < kPlan; ++k) {
+      for (int k = 0; k < kPlanItems; ++k) {
         const int e = pfirst + k * pstride;
         if (e < n) {
           const int r = e / hw, jl = w * (e - r * hw);
-          const int b = r / 3, gi = r - 3 * b;
-          plan_dst[k] = r * Hc + jl;
-          plan_src[k] = src0 + (size_t)b * T * 3 * H + gi * H + jl;
+          const int b = cpe == 3 ? r : r / 3, gi0 = cpe == 3 ? 0 : r - 3 * b;
+          plan_dst[k] = (b * 3 + gi0) * Hc + jl;
+          plan_off[k] = b * T * 3 * H + gi0 * H + jl;
           plan_n = k + 1;
         }
       }
@@ -301,14 +307,18 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
       return;
     }
     float* dst = ring + (s % pd) * ring_stride;
-    const size_t so = (size_t)s * 3 * H;
+    const float* src = G_c + (size_t)s * 3 * H;
 #pragma unroll
-    for (int k = 0; k < kPlan; ++k) {
+    for (int k = 0; k < kPlanItems; ++k) {
       if (k < plan_n) {
-        if (vec4)
-          cp_async16(dst + plan_dst[k], plan_src[k] + so);
-        else
-          cp_async4(dst + plan_dst[k], plan_src[k] + so);
+        float* d = dst + plan_dst[k];
+        const float* g = src + plan_off[k];
+        for (int gi = 0; gi < cpe; ++gi) {
+          if (vec4)
+            cp_async16(d + gi * Hc, g + gi * H);
+          else
+            cp_async4(d + gi * Hc, g + gi * H);
+        }
       }
     }
   };
@@ -515,36 +525,40 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
     cp_async_commit();
   }
   // Per-thread plan of the time loop's prefetch copies (as in the forward).
-  // Source of a copy at time s: plan_src + s * plan_ss (H for dout, 5H for
-  // the stash).
+  // Entry k: inputs q0 .. q0 + cpe - 1 of row b, units jl .. jl + w - 1, to
+  // ring offsets plan_dst[k] + q * Hc; input 0 (dout) comes from
+  // dout_c + s * H + plan_offd[k], input q >= 1 from
+  // stash_c + s * 5H + plan_offs[k] + (q - 1) * H.  cpe is 1, 2, 3 or 6: the
+  // smallest that keeps every thread at kPlanItems entries or fewer.
   const int ns_last = nb - ((nb - 1) / R) * R;
   const int nact_last = ns_last * hcnt;
   const bool idle_issue = nact_last < nthr;
   const int pfirst = idle_issue ? tid - nact_last : tid, pstride = idle_issue ? nthr - nact_last : nthr;
-  int plan_n = 0;
-  int plan_dst[kPlan], plan_ss[kPlan];
-  const float* plan_src[kPlan];
+  int plan_n = 0, cpe = 1, plan_q0[kPlanItems];
+  int plan_dst[kPlanItems], plan_offd[kPlanItems], plan_offs[kPlanItems];
+  const float* const dout_c = a.dout ? a.dout + (size_t)b_begin * T * H + j0 : nullptr;
+  const float* const stash_c = a.stash + (size_t)b_begin * T * 5 * H + j0;
   {
     const int w = vec4 ? 4 : 1;
-    const int hw = hcnt / w, n = nb * 6 * hw;
+    const int hw = hcnt / w;
 #pragma unroll
-    for (int k = 0; k < kPlan; ++k) {
-      plan_dst[k] = 0;
-      plan_ss[k] = 0;
-      plan_src[k] = a.stash;
-    }
-    if (a.dout == nullptr || (pfirst >= 0 && pfirst + kPlan * pstride < n)) plan_n = -1;
+    for (int k = 0; k < kPlanItems; ++k) plan_dst[k] = plan_offd[k] = plan_offs[k] = plan_q0[k] = 0;
+    while (cpe < 6 && nb * (6 / cpe) * hw > kPlanItems * pstride) cpe = cpe == 1 ? 2 : (cpe == 2 ? 3 : 6);
+    const int per = 6 / cpe, n = nb * per * hw;
+    if (a.dout == nullptr || (pfirst >= 0 && pfirst + kPlanItems * pstride < n) ||
+        (size_t)nb * T * 5 * H >= (1ull << 31))
+      plan_n = -1;
     if (pfirst >= 0 && plan_n == 0) {
 #pragma unroll
-      for (int k = 0; k < kPlan; ++k) {
+      for (int k = 0; k < kPlanItems; ++k) {
         const int e = pfirst + k * pstride;
         if (e < n) {
           const int r = e / hw, jl = w * (e - r * hw);
-          const int b = r / 6, q = r - 6 * b;
-          const size_t row0 = (size_t)(b_begin + b) * T;
-          plan_dst[k] = r * Hc + jl;
-          plan_src[k] = q == 0 ? a.dout + row0 * H + j0 + jl : a.stash + row0 * 5 * H + (q - 1) * H + j0 + jl;
-          plan_ss[k] = q == 0 ? H : 5 * H;
+          const int b = r / per, q0 = (r - per * b) * cpe;
+          plan_q0[k] = q0;
+          plan_dst[k] = (b * 6 + q0) * Hc + jl;
+          plan_offd[k] = b * T * H + jl;
+          plan_offs[k] = b * T * 5 * H + jl;
           plan_n = k + 1;
         }
       }
@@ -557,14 +571,20 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
     }
     const int s = T - 1 - it;
     float* dst = ring + (it % pd) * ring_stride;
+    const float* src_d = dout_c + (size_t)s * H;
+    const float* src_s = stash_c + (size_t)s * 5 * H;
 #pragma unroll
-    for (int k = 0; k < kPlan; ++k) {
+    for (int k = 0; k < kPlanItems; ++k) {
       if (k < plan_n) {
-        const float* src = plan_src[k] + (size_t)s * plan_ss[k];
-        if (vec4)
-          cp_async16(dst + plan_dst[k], src);
-        else
-          cp_async4(dst + plan_dst[k], src);
+        float* d = dst + plan_dst[k];
+        for (int c = 0; c < cpe; ++c) {
+          const int q = plan_q0[k] + c;
+          const float* src = q == 0 ? src_d + plan_offd[k] : src_s + plan_offs[k] + (q - 1) * H;
+          if (vec4)
+            cp_async16(d + c * Hc, src);
+          else
+            cp_async4(d + c * Hc, src);
+        }
       }
     }
   };
