@@ -74,3 +74,66 @@ class DataParallelTrainer:
         with torch.no_grad():
             self.flat.add_(self.grad, alpha=-self.lr / self.world)
         return loss.detach()
+
+
+class HostBatchPrefetcher:
+    """Double-buffered host-to-device staging of training batches.
+
+    ``put(*host_tensors)`` starts copying one batch (pinned host tensors, for
+    truly asynchronous copies) into the idle one of two device buffer sets, on
+    a dedicated copy stream; ``get()`` makes the current (compute) stream wait
+    for the oldest outstanding copy and returns its device tensors.  Calling
+    ``put`` for batch k+1 right after ``get`` for batch k overlaps that copy
+    with step k's kernels, as a pinned-memory data loader does.
+
+    A buffer set is refilled only after the compute stream has finished the
+    step that read it: ``get`` records that point (after the previous step's
+    work was enqueued) and ``put`` makes the copy stream wait for it.
+    """
+
+    def __init__(self, device: torch.device, copy_stream: Optional[torch.cuda.Stream] = None) -> None:
+        self.device = torch.device(device)
+        self.stream = copy_stream if copy_stream is not None else torch.cuda.Stream(self.device)
+        self._bufs: list = [None, None]
+        self._ready: list = [None, None]
+        self._free: list = [None, None]
+        self._fill = 0          # slot the next put() fills
+        self._queue: list = []  # slots filled, not yet handed out
+        self._in_use: Optional[int] = None
+
+    def put(self, *host: torch.Tensor) -> None:
+        if len(self._queue) >= 2:
+            raise RuntimeError("HostBatchPrefetcher holds two batches already; call get() first")
+        slot = self._fill
+        self._fill ^= 1
+        bufs = self._bufs[slot]
+        if bufs is None or len(bufs) != len(host) or any(
+                b.shape != h.shape or b.dtype != h.dtype for b, h in zip(bufs, host)):
+            # allocated on the current stream and kept for the object's lifetime
+            bufs = tuple(torch.empty(h.shape, dtype=h.dtype, device=self.device) for h in host)
+            self._bufs[slot] = bufs
+            self.stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(self.stream):
+            if self._free[slot] is not None:
+                self.stream.wait_event(self._free[slot])
+            for d, h in zip(bufs, host):
+                d.copy_(h, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(self.stream)
+        self._ready[slot] = ev
+        self._queue.append(slot)
+
+    def get(self):
+        if not self._queue:
+            raise RuntimeError("HostBatchPrefetcher.get() without a pending put()")
+        cur = torch.cuda.current_stream(self.device)
+        if self._in_use is not None:
+            # everything enqueued so far (the previous step) has read that slot
+            ev = torch.cuda.Event()
+            ev.record(cur)
+            self._free[self._in_use] = ev
+        slot = self._queue.pop(0)
+        cur.wait_event(self._ready[slot])
+        self._in_use = slot
+        bufs = self._bufs[slot]
+        return bufs if len(bufs) != 1 else bufs[0]
