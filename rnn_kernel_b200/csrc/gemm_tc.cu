@@ -148,7 +148,10 @@ struct Smem {
   static constexpr int kBTile = BN * kBK * 4;
   static constexpr int kStage = 2 * kATile + 2 * kBTile;  // A hi, A lo, B hi, B lo
   static constexpr int kBarOff = S * kStage;
-  static constexpr int kBytes = kBarOff + 256 + 1024;  // + barriers + alignment slack
+  // per drain warp a 32 x 16 epilogue staging block (row pitch 17 floats)
+  static constexpr int kEpiPitch = 17;
+  static constexpr int kEpiOff = kBarOff + 256;
+  static constexpr int kBytes = kEpiOff + kDrainWarps * 32 * kEpiPitch * 4 + 1024;  // + alignment slack
 };
 
 // Accumulation.  The tensor cores' FP32 accumulation truncates instead of
@@ -362,19 +365,34 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ah, const __grid_cons
       const int n0 = w.n0 + kCW * chalf;
       float* Cu = splits > 1 ? C + (long)w.split * M * ldc : C;
       const float* bu = splits > 1 ? nullptr : bias;
-      if (row < M) {
-        float* crow = Cu + (long)row * ldc + n0;
-        const bool vec = (ldc % 4 == 0) && n0 + kCW <= N && ((reinterpret_cast<uintptr_t>(crow) & 15) == 0);
-        if (vec) {
+      // Warp-uniform: 16-byte rows, whole 64-column block inside N.
+      const bool vec = (ldc % 4 == 0) && n0 + kCW <= N && ((reinterpret_cast<uintptr_t>(Cu + n0) & 15) == 0);
+      if (vec) {
+        // Each lane holds one row; stage 16 columns at a time through this
+        // warp's shared block and store them with 4 lanes per row (64
+        // contiguous bytes, 8 rows per instruction) instead of one 16-byte
+        // piece of 32 different rows per instruction.
+        float* eb = reinterpret_cast<float*>(smem + L::kEpiOff) + (warp - 2) * (32 * L::kEpiPitch);
+        const int rbase = w.m0 + 32 * quarter;
 #pragma unroll
-          for (int c = 0; c < kCW; c += 4) {
-            float4 v = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
-            if (bu) {
-              v.x += bu[n0 + c]; v.y += bu[n0 + c + 1]; v.z += bu[n0 + c + 2]; v.w += bu[n0 + c + 3];
+        for (int c0 = 0; c0 < kCW; c0 += 16) {
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) eb[lane * L::kEpiPitch + jj] = acc[c0 + jj] + (bu ? bu[n0 + c0 + jj] : 0.0f);
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int r = i * 8 + (lane >> 2), cc = (lane & 3) * 4;
+            if (rbase + r < M) {
+              const float* e = eb + r * L::kEpiPitch + cc;
+              *reinterpret_cast<float4*>(Cu + (long)(rbase + r) * ldc + n0 + c0 + cc) =
+                  make_float4(e[0], e[1], e[2], e[3]);
             }
-            *reinterpret_cast<float4*>(crow + c) = v;
           }
-        } else {
+          __syncwarp();
+        }
+      } else if (row < M) {
+        float* crow = Cu + (long)row * ldc + n0;
+        {
 #pragma unroll
           for (int c = 0; c < kCW; ++c) {
             const int n = n0 + c;
