@@ -173,6 +173,16 @@ def step_roofline_ms(b, T, H, sm_mhz: float, sms: int = 148) -> float:
     return 1e3 * T * (t_f + t_b)
 
 
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except ValueError:
+            return {}
+    return {}
+
+
 def load_traffic():
     p = ROOT / "profiles" / "ncu_traffic.json"
     if p.exists():
@@ -253,10 +263,11 @@ def main():
     torch.cuda.synchronize()
     barrier()
     ms = sum(times) / K
+    med = sorted(times)[K // 2] if K % 2 else 0.5 * (sorted(times)[K // 2 - 1] + sorted(times)[K // 2])
     if world > 1:
-        t = torch.tensor([ms], device=dev)
+        t = torch.tensor([ms, med], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t)
+        ms, med = float(t[0]), float(t[1])
     clocks = clk.summary()
     value = B * world * T / (ms / 1e3)
 
@@ -337,12 +348,28 @@ def main():
         "flops_per_launch": flops,
     }
     t_roof = step_roofline_ms(B, T, H, 1965.0) * L
+    # Side-by-side bounds: + the step's tensor-core products at 3xTF32
+    # (nominal 1.1 PFLOP/s TF32 / 3 passes), and the minimal HBM traffic of a
+    # step (~(12 I + 132 H) bytes per sample-timestep per layer) at the
+    # measured copy bandwidth.
+    gemm_flop = 0.0
+    for l in range(L):
+        li = I if l == 0 else H
+        n_prod = 3 if l == 0 else 4  # projection, dW_ih, dW_hh (+ dx into the layer below)
+        gemm_flop += n_prod * 2.0 * B * T * 3 * H * li
+    t_gemm = gemm_flop / (1.1e15 / 3) * 1e3
+    hbm_gbs = measured_peaks().get("hbm_gbs") or 6650.0
+    hbm_bytes = sum((12 * (I if l == 0 else H) + 132 * H) * B * T for l in range(L))
     step_roof = {"t_roof_ms": t_roof, "frac": t_roof / ms,
-                 "definition": "T*(t_fwd+t_bwd), t = 3H^2*4B/SMEM_BW + (2*b*3H*H + {10|16}*b*H)/P_fp32, nominal peaks"}
+                 "definition": "T*(t_fwd+t_bwd), t = 3H^2*4B/SMEM_BW + (2*b*3H*H + {10|16}*b*H)/P_fp32, nominal peaks",
+                 "full_step_bound_ms": t_roof + t_gemm, "full_step_frac": (t_roof + t_gemm) / ms,
+                 "gemm_gflop_per_step": gemm_flop / 1e9,
+                 "hbm_bound_ms": hbm_bytes / (hbm_gbs * 1e9) * 1e3, "hbm_bytes_per_step": hbm_bytes,
+                 "hbm_peak_gbs": hbm_gbs}
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
-        "ms_per_step": ms, "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
+        "ms_per_step": ms, "median_ms_per_step": med, "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
         "dtype": "fp32", "data": "synthetic: x, target ~ N(0,1) per rank (seed 1000+rank); weights U(-1/16,1/16)",
         "config": {"workload": f"gru_train_step 1-layer I={I} H={H} T={T}, batch {B}/GPU "
                                f"(fwd + MSE + bwd + allreduce + SGD lr 1e-2)",
@@ -384,10 +411,10 @@ def main():
     if world == 1 and not args.no_cpu_baseline:
         from oracle.cpu_baseline import time_cpu_train_step
 
-        r = time_cpu_train_step(B, T, I, H, warmup=1, steps=2)
+        r = time_cpu_train_step(B, T, I, H, warmup=1, steps=3)
         line["cpu_baseline"] = {"value": r["value"], "unit": UNIT, "cores": r["cores"], "kind": "reference",
                                 "sample": f"torch.nn.GRU FP32 train step on host CPU ({r['cpu_model']}), "
-                                          f"full B={B},T={T} workload, 1 warm-up + 2 timed steps"}
+                                          f"full B={B},T={T} workload, 1 warm-up + 3 timed steps"}
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -13,11 +13,17 @@ layer's gradients into that buffer in place, so a step is::
     flat_params.add_(grad, alpha=-lr / world)  # SGD on the mean gradient
 
 i.e. one collective and one fused update kernel per step, independent of the
-number of layers.  The module is any ``nn.Module`` (the B200 :class:`GRU` on
+number of layers.  With ``overlap=True`` (default) and several layers, the
+gradient buffer is reduced per layer instead: each layer's slice is
+all-reduced asynchronously as soon as autograd has accumulated all of its
+gradients (a post-accumulate-grad hook per parameter), so the upper layers'
+reductions run while the lower layers' backward still computes; the update
+waits for all of them.  The module is any ``nn.Module`` (the B200 :class:`GRU` on
 GPUs; ``torch.nn.GRU`` on CPU ``gloo`` ranks in the tests of this logic).
 """
 from __future__ import annotations
 
+import re
 from typing import Optional
 
 import torch
@@ -50,15 +56,54 @@ class DataParallelTrainer:
     """SGD data-parallel trainer: shard-local fwd/bwd, one all-reduce, one update."""
 
     def __init__(self, module: nn.Module, lr: float = 1e-2,
-                 process_group: Optional[dist.ProcessGroup] = None) -> None:
+                 process_group: Optional[dist.ProcessGroup] = None, overlap: bool = True) -> None:
         self.module = module
         self.lr = float(lr)
         self.group = process_group
         self.world = dist.get_world_size(process_group) if dist.is_available() and dist.is_initialized() else 1
         self.flat, self.grad = flatten_parameters_(module)
+        self._buckets: list = []   # [lo, hi) slices of the gradient buffer, one per layer
+        self._pending: list = []   # parameters of each bucket not yet accumulated this step
+        self._works: list = []
+        self._in_step = False
         if self.world > 1:
             # Every rank starts from rank 0's weights.
             dist.broadcast(self.flat, src=0, group=process_group)
+            if overlap:
+                self._install_bucket_hooks()
+
+    def _install_bucket_hooks(self) -> None:
+        # Group the parameters by the layer suffix of their names (``_l{k}``,
+        # nn.GRU convention); a layer's parameters must be contiguous in the
+        # flat buffer.  One bucket only: nothing to overlap, keep one call.
+        layers: dict = {}
+        off = 0
+        for name, p in self.module.named_parameters():
+            if not p.requires_grad:
+                continue
+            m = re.search(r"_l(\d+)", name)
+            key = int(m.group(1)) if m else -1
+            lo, hi, ps = layers.get(key, (off, off, []))
+            if hi != off:
+                return  # not contiguous
+            layers[key] = (lo, off + p.numel(), ps + [p])
+            off += p.numel()
+        if len(layers) < 2:
+            return
+        for b, (lo, hi, ps) in enumerate(layers.values()):
+            self._buckets.append((lo, hi, len(ps)))
+            for p in ps:
+                p.register_post_accumulate_grad_hook(lambda _p, b=b: self._param_ready(b))
+        self._pending = [n for _, _, n in self._buckets]
+
+    def _param_ready(self, b: int) -> None:
+        if not self._in_step:
+            return  # a backward outside step(): leave the gradients alone
+        self._pending[b] -= 1
+        if self._pending[b] == 0:
+            lo, hi, _ = self._buckets[b]
+            self._works.append(
+                dist.all_reduce(self.grad[lo:hi], op=dist.ReduceOp.SUM, group=self.group, async_op=True))
 
     def loss(self, x: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
         out, _ = self.module(x)
@@ -67,9 +112,24 @@ class DataParallelTrainer:
     def step(self, x: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
         """One train step on this rank's shard; returns the shard loss (detached)."""
         self.grad.zero_()
+        if self._buckets:
+            self._pending = [n for _, _, n in self._buckets]
+            self._works = []
         loss = self.loss(x, target)
-        loss.backward()
-        if self.world > 1:
+        self._in_step = True
+        try:
+            loss.backward()
+        finally:
+            self._in_step = False
+        if self.world > 1 and self._buckets:
+            for w in self._works:
+                w.wait()
+            # a layer whose parameters got no gradient this step
+            for (lo, hi, _), left in zip(self._buckets, self._pending):
+                if left > 0:
+                    dist.all_reduce(self.grad[lo:hi], op=dist.ReduceOp.SUM, group=self.group)
+            self._works = []
+        elif self.world > 1:
             dist.all_reduce(self.grad, op=dist.ReduceOp.SUM, group=self.group)
         with torch.no_grad():
             self.flat.add_(self.grad, alpha=-self.lr / self.world)

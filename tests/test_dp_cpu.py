@@ -33,13 +33,14 @@ def _shard(rank, step, b):
     return torch.randn(b, T, I, generator=g), torch.randn(b, T, H, generator=g)
 
 
-def _worker(rank, world, port, out_path):
+def _worker(rank, world, port, out_path, layers=1, overlap=True):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     torch.manual_seed(0 if rank == 0 else 99)  # weights differ until the broadcast
-    model = torch.nn.GRU(I, H, batch_first=True)
-    tr = DataParallelTrainer(model, lr=LR)
+    model = torch.nn.GRU(I, H, num_layers=layers, batch_first=True)
+    tr = DataParallelTrainer(model, lr=LR, overlap=overlap)
+    assert bool(tr._buckets) == (overlap and layers > 1)
     losses = []
     for step in range(STEPS):
         x, y = _shard(rank, step, GLOBAL_B // world)
@@ -52,9 +53,9 @@ def _worker(rank, world, port, out_path):
     dist.destroy_process_group()
 
 
-def _single(world):
+def _single(world, layers=1):
     torch.manual_seed(0)
-    model = torch.nn.GRU(I, H, batch_first=True)
+    model = torch.nn.GRU(I, H, num_layers=layers, batch_first=True)
     tr = DataParallelTrainer(model, lr=LR)
     losses = []
     for step in range(STEPS):
@@ -77,13 +78,16 @@ def test_flatten_parameters_views():
 
 
 @pytest.mark.timeout(300)
-def test_dp_gloo_two_ranks_matches_single_process():
+@pytest.mark.parametrize("layers,overlap", [(1, True), (2, True), (2, False)])
+def test_dp_gloo_two_ranks_matches_single_process(layers, overlap):
+    # layers=2, overlap=True: per-layer buckets all-reduced asynchronously
+    # from post-accumulate-grad hooks while the lower layer's backward runs.
     world = 2
     with tempfile.TemporaryDirectory() as d:
         path = os.path.join(d, "r0.pt")
-        mp.spawn(_worker, args=(world, _free_port(), path), nprocs=world, join=True)
+        mp.spawn(_worker, args=(world, _free_port(), path, layers, overlap), nprocs=world, join=True)
         res = torch.load(path)
-    flat1, losses1 = _single(world)
+    flat1, losses1 = _single(world, layers)
     torch.testing.assert_close(res["flat"], flat1, rtol=1e-5, atol=1e-6)
     for a, b in zip(res["losses"], losses1):
         assert abs(a - b) <= 1e-5 * max(1.0, abs(b))

@@ -31,15 +31,16 @@ def _shard(rank, step, b, dev):
     return torch.randn(b, T, I, generator=g).to(dev), torch.randn(b, T, H, generator=g).to(dev)
 
 
-def _worker(rank, world, port, out_path):
+def _worker(rank, world, port, out_path, layers=1):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
     from rnn_kernel_b200 import GRU, DataParallelTrainer
 
     torch.manual_seed(0)
-    model = GRU(I, H).cuda()
+    model = GRU(I, H, num_layers=layers).cuda()
     tr = DataParallelTrainer(model, lr=LR)
+    assert bool(tr._buckets) == (layers > 1)  # per-layer overlapped all-reduce
     losses = []
     for step in range(STEPS):
         x, y = _shard(rank, step, GLOBAL_B // world, "cuda")
@@ -52,16 +53,17 @@ def _worker(rank, world, port, out_path):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_dp_two_gpus_matches_single_gpu():
+@pytest.mark.parametrize("layers", [1, 2])
+def test_dp_two_gpus_matches_single_gpu(layers):
     from rnn_kernel_b200 import GRU, DataParallelTrainer
 
     world = 2
     with tempfile.TemporaryDirectory() as d:
         path = os.path.join(d, "r0.pt")
-        mp.spawn(_worker, args=(world, _free_port(), path), nprocs=world, join=True)
+        mp.spawn(_worker, args=(world, _free_port(), path, layers), nprocs=world, join=True)
         res = torch.load(path)
     torch.manual_seed(0)
-    model = GRU(I, H).cuda()
+    model = GRU(I, H, num_layers=layers).cuda()
     tr = DataParallelTrainer(model, lr=LR)
     losses = []
     for step in range(STEPS):
