@@ -73,15 +73,17 @@ inline int pad4(int v) { return (v + 3) / 4 * 4; }
 struct FwdLayout {
   size_t g, xh, xl, wh, wl, total;
   int ldx;  // row stride of the split x / W_ih copies (I rounded up to 4)
+  int ldg;  // row stride of the input gates G (3H rounded up to 4: 16-byte rows)
 };
 
 FwdLayout fwd_layout(int B, int T, int I, int H) {
   const long BT = (long)B * T;
   FwdLayout l{};
   l.ldx = pad4(I);
+  l.ldg = pad4(3 * H);
   size_t off = 0;
   l.g = off;
-  off = align_up(off + sizeof(float) * BT * 3 * H, kAlign);
+  off = align_up(off + sizeof(float) * BT * l.ldg, kAlign);
   l.xh = off;
   off = align_up(off + sizeof(float) * BT * l.ldx, kAlign);
   l.xl = off;
@@ -241,11 +243,11 @@ int gru_forward(const float* x, const float* h0, const float* w_ih, const float*
   // G = x . W_ih^T + b_ih on the tensor cores (3xTF32, pre-split operands).
   if ((rc = split_tf32(x, (long)B * T, I, I, xh, xl, l.ldx, stream))) return rc;
   if ((rc = split_tf32(w_ih, 3L * H, I, I, wh, wl, l.ldx, stream))) return rc;
-  TcGemmArgs ga{xh, l.ldx, wh, l.ldx, G, 3 * H, b_ih, B * T, 3 * H, I, false, false, xl, wl};
+  TcGemmArgs ga{xh, l.ldx, wh, l.ldx, G, l.ldg, b_ih, B * T, 3 * H, I, false, false, xl, wl};
   if ((rc = tc_gemm(ga, stream, kKindInputGemm))) return rc;
   RecGeom g{};
   if ((rc = geometry(0, B, T, H, dev, &g))) return rc;
-  return launch_rec_forward(G, h0, w_hh, b_hh, out, hn, stash, g, stream);
+  return launch_rec_forward(G, l.ldg, h0, w_hh, b_hh, out, hn, stash, g, stream);
 }
 
 int gru_backward(const float* dout, const float* dhn, const float* x, const float* w_ih,

@@ -58,7 +58,8 @@ int wait_probe(unsigned long long limit_ns, int* result_dev, cudaStream_t stream
 int rec_forward_geometry(int B, int T, int H, int device, RecGeom* g);
 int rec_backward_geometry(int B, int T, int H, int device, RecGeom* g);
 
-int launch_rec_forward(const float* G, const float* h0, const float* w_hh, const float* b_hh,
+// G: input gates [B*T rows, 3H], row stride ldg floats.
+int launch_rec_forward(const float* G, int ldg, const float* h0, const float* w_hh, const float* b_hh,
                        float* out, float* hn, float* stash, const RecGeom& g,
                        cudaStream_t stream);
 // dG_ih / dG_hh are written pre-split (hi, lo) with row stride ldgi.

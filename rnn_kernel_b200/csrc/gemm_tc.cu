@@ -582,7 +582,8 @@ int tc_splits(const TcGemmArgs& a, int device) {
 
 size_t tc_gemm_ws_bytes(const TcGemmArgs& a, int device) {
   const int s = tc_splits(a, device);
-  return s > 1 ? sizeof(float) * (size_t)s * a.M * a.N : 0;
+  // partials [s][M][N rounded up to 4 floats]: 16-byte rows for the epilogue
+  return s > 1 ? sizeof(float) * (size_t)s * a.M * ((a.N + 3) / 4 * 4) : 0;
 }
 
 int tc_gemm(const TcGemmArgs& a, cudaStream_t stream, int kind, void* ws, size_t ws_bytes) {
@@ -603,7 +604,7 @@ int tc_gemm(const TcGemmArgs& a, cudaStream_t stream, int kind, void* ws, size_t
       return GRU_ERR_INVALID;
     }
     C = static_cast<float*>(ws);
-    ldc = a.N;
+    ldc = (a.N + 3) / 4 * 4;
   }
   LaunchScope scope(kind, stream, splits > 1 ? 2 : 1);
   int rc;
@@ -619,7 +620,7 @@ int tc_gemm(const TcGemmArgs& a, cudaStream_t stream, int kind, void* ws, size_t
       set_error("tc_gemm: bias with split-K is not supported");
       return GRU_ERR_INVALID;
     }
-    splitk_sum_kernel<<<sm_count(dev) * 4, 256, 0, stream>>>(C, splits, a.M, a.N, a.N, a.C, a.ldc);
+    splitk_sum_kernel<<<sm_count(dev) * 4, 256, 0, stream>>>(C, splits, a.M, a.N, ldc, a.C, a.ldc);
     GRU_CUDA_TRY(cudaGetLastError());
   }
   return GRU_OK;

@@ -160,7 +160,7 @@ constexpr int kPlanItems = 2;
 __device__ __forceinline__ uint32_t phase_parity(int it) { return (uint32_t)((((it + 1) >> 1) - 1) & 1); }
 
 struct FwdArgs {
-  const float* G;     // [B,T,3H] input gates (x.W_ih^T + b_ih)
+  const float* G;     // [B,T,3H] input gates (x.W_ih^T + b_ih), row stride 3H rounded up to 4
   const float* h0;    // [B,H]
   const float* w_hh;  // [3H,H]
   const float* b_hh;  // [3H]
@@ -182,6 +182,7 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
   const int nthr = blockDim.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int H = g.H, T = g.T, Hc = g.Hc, Kp = g.nw * 32, bcp = g.bcp, pd = g.pd;
+  const int ldg = (3 * H + 3) & ~3;  // row stride of G
   const int j0 = c * Hc;
   const int hcnt = max(1, min(Hc, H - j0));
   // first pointwise item of this thread (row, unit) in a sub-chunk
@@ -240,8 +241,8 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
   const bool vec4 = g.vec4 != 0;
   auto issue = [&](int s, int first, int stride) {
     float* dst = ring + (s % pd) * ring_stride;
-    const float* src = a.G + ((size_t)b_begin * T + s) * 3 * H + j0;
-    const size_t bstride = (size_t)T * 3 * H;
+    const float* src = a.G + ((size_t)b_begin * T + s) * ldg + j0;
+    const size_t bstride = (size_t)T * ldg;
     if (vec4) {
       const int h4 = hcnt >> 2, n = nb * 3 * h4;
       for (int e = first; e < n; e += stride) {
@@ -277,7 +278,7 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
   // thread at kPlanItems entries or fewer.
   int plan_n = 0, cpe = 1;
   int plan_dst[kPlanItems], plan_off[kPlanItems];
-  const float* const G_c = a.G + (size_t)b_begin * T * 3 * H + j0;
+  const float* const G_c = a.G + (size_t)b_begin * T * ldg + j0;
   {
     const int w = vec4 ? 4 : 1;
     const int hw = hcnt / w;
@@ -286,7 +287,7 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
     if (pstride > 0 && nb * 3 * hw > kPlanItems * pstride) cpe = 3;
     const int n = nb * (3 / cpe) * hw;
     // more than kPlanItems entries, or offsets beyond 32 bits: no plan
-    if ((pfirst >= 0 && pfirst + kPlanItems * pstride < n) || (size_t)nb * T * 3 * H >= (1ull << 31)) plan_n = -1;
+    if ((pfirst >= 0 && pfirst + kPlanItems * pstride < n) || (size_t)nb * T * ldg >= (1ull << 31)) plan_n = -1;
     if (pfirst >= 0 && plan_n == 0) {
 #pragma unroll
       for (int k = 0; k < kPlanItems; ++k) {
@@ -295,7 +296,7 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
           const int r = e / hw, jl = w * (e - r * hw);
           const int b = cpe == 3 ? r : r / 3, gi0 = cpe == 3 ? 0 : r - 3 * b;
           plan_dst[k] = (b * 3 + gi0) * Hc + jl;
-          plan_off[k] = b * T * 3 * H + gi0 * H + jl;
+          plan_off[k] = b * T * ldg + gi0 * H + jl;
           plan_n = k + 1;
         }
       }
@@ -307,7 +308,7 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
       return;
     }
     float* dst = ring + (s % pd) * ring_stride;
-    const float* src = G_c + (size_t)s * 3 * H;
+    const float* src = G_c + (size_t)s * ldg;
 #pragma unroll
     for (int k = 0; k < kPlanItems; ++k) {
       if (k < plan_n) {
@@ -910,9 +911,13 @@ int rec_backward_geometry(int B, int T, int H, int device, RecGeom* g) {
   return finish_geometry(g, device, false, bwd_smem);
 }
 
-int launch_rec_forward(const float* G, const float* h0, const float* w_hh, const float* b_hh,
+int launch_rec_forward(const float* G, int ldg, const float* h0, const float* w_hh, const float* b_hh,
                        float* out, float* hn, float* stash, const RecGeom& g,
                        cudaStream_t stream) {
+  if (ldg != ((3 * g.H + 3) & ~3)) {
+    set_error("internal: input-gate row stride must be 3H rounded up to 4");
+    return GRU_ERR_INVALID;
+  }
   FwdArgs a{G, h0, w_hh, b_hh, out, hn, stash};
   RecGeom gg = g;
   if (reinterpret_cast<uintptr_t>(G) & 15) gg.vec4 = 0;  // 16-byte copies need an aligned base
