@@ -21,24 +21,33 @@ __global__ void bias_grad_partial_kernel(const float* __restrict__ dgi, const fl
   const float* X = col < 3 * H ? dgi + col : dgh + (col - H);
   const float* Y = col < 3 * H ? dgi_lo + col : dgh_lo + (col - H);
   const long r0 = blockIdx.y * rchunk, r1 = min(rows, r0 + rchunk);
+  // four rows per iteration: eight independent loads in flight per thread
   double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
   long r = r0;
-  for (; r + 2 <= r1; r += 2) {
-    s0 += X[r * ld];
-    s1 += Y[r * ld];
-    s2 += X[(r + 1) * ld];
-    s3 += Y[(r + 1) * ld];
+  for (; r + 4 <= r1; r += 4) {
+    const float x0 = X[r * ld], y0 = Y[r * ld], x1 = X[(r + 1) * ld], y1 = Y[(r + 1) * ld];
+    const float x2 = X[(r + 2) * ld], y2 = Y[(r + 2) * ld], x3 = X[(r + 3) * ld], y3 = Y[(r + 3) * ld];
+    s0 += (double)x0 + (double)y0;
+    s1 += (double)x1 + (double)y1;
+    s2 += (double)x2 + (double)y2;
+    s3 += (double)x3 + (double)y3;
   }
   for (; r < r1; ++r) s0 += (double)X[r * ld] + (double)Y[r * ld];
   part[(long)blockIdx.y * 4 * H + col] = (s0 + s1) + (s2 + s3);
 }
 
+// One warp per column: lane l sums chunks l, l+32, ... then a fixed shuffle
+// tree (deterministic).
 __global__ void bias_grad_final_kernel(const double* __restrict__ part, int nchunks, int H, float* __restrict__ db_ih,
                                        float* __restrict__ db_hh) {
-  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  const int col = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
   if (col >= 4 * H) return;
   double s = 0.0;
-  for (int z = 0; z < nchunks; ++z) s += part[(long)z * 4 * H + col];
+  for (int z = lane; z < nchunks; z += 32) s += part[(long)z * 4 * H + col];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane != 0) return;
   const float v = (float)s;
   if (col < 3 * H) db_ih[col] = v;
   if (col < 2 * H) db_hh[col] = v;
@@ -84,7 +93,7 @@ int bias_grads(const float* dgi, const float* dgi_lo, const float* dgh, const fl
   bias_grad_partial_kernel<<<grid, 128, 0, stream>>>(dgi, dgi_lo, dgh, dgh_lo, rows, H, ld, rchunk > 0 ? rchunk : 1,
                                                    part);
   GRU_CUDA_TRY(cudaGetLastError());
-  bias_grad_final_kernel<<<ceil_div(4 * H, 128), 128, 0, stream>>>(part, kColChunks, H, db_ih, db_hh);
+  bias_grad_final_kernel<<<ceil_div(4 * H, 8), 256, 0, stream>>>(part, kColChunks, H, db_ih, db_hh);
   GRU_CUDA_TRY(cudaGetLastError());
   return GRU_OK;
 }
