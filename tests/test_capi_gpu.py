@@ -31,28 +31,38 @@ def _case(B, T, I, H, seed):
     return {k2: f32(v) for k2, v in dict(x=x, h0=h0, dout=dout, dhn=dhn, **w).items()}
 
 
-@pytest.mark.parametrize("B,T,I,H", [(3, 7, 5, 33), (4, 16, 64, 256), (2, 5, 3, 129), (17, 4, 2, 20)])
-@pytest.mark.parametrize("with_dout", [True, False])
-def test_capi_forward_backward_vs_oracle(B, T, I, H, with_dout):
+def _run_capi(B, T, I, H, with_dout, offset=0, seed=None):
+    """Forward + backward through the C ABI vs the FP64 oracle.  With offset k
+    every caller-owned buffer starts k floats into its allocation (k = 1:
+    4-byte aligned only, so every 16-byte fast path must step aside)."""
     lib = _lib.load()
-    c = _case(B, T, I, H, seed=B * 1000 + H)
+    c = _case(B, T, I, H, seed=B * 1000 + H if seed is None else seed)
     # Oracle in float64 on the float32-rounded inputs.
     d64 = {k: v.astype(np.float64) for k, v in c.items()}
     out_o, hn_o, st = O.gru_layer_forward(d64["x"], d64["h0"], d64["w_ih"], d64["w_hh"], d64["b_ih"], d64["b_hh"])
     g = O.gru_layer_backward(d64["dout"] if with_dout else None, d64["dhn"], d64["x"], d64["w_ih"], d64["w_hh"], st)
 
     dev = torch.device("cuda")
-    t = {k: torch.from_numpy(v).to(dev) for k, v in c.items()}
-    out = torch.empty(B, T, H, device=dev)
-    hn = torch.empty(B, H, device=dev)
-    stash = torch.empty(lib.gru_stash_bytes(B, T, H) // 4, device=dev)
+
+    def buf(*shape, like=None):
+        n = int(np.prod(shape))
+        base = torch.empty(n + offset, device=dev)
+        v = base[offset:].view(*shape)
+        if like is not None:
+            v.copy_(torch.from_numpy(like))
+        return v
+
+    t = {k: buf(*v.shape, like=v) for k, v in c.items()}
+    out = buf(B, T, H)
+    hn = buf(B, H)
+    stash = buf(lib.gru_stash_bytes(B, T, H) // 4)
     wsf = lib.gru_forward_workspace_bytes(B, T, I, H)
     ws = torch.empty(wsf, dtype=torch.uint8, device=dev)
     s = torch.cuda.current_stream().cuda_stream
     rc = lib.gru_forward(_p(t["x"]), _p(t["h0"]), _p(t["w_ih"]), _p(t["w_hh"]), _p(t["b_ih"]), _p(t["b_hh"]),
                          _p(out), _p(hn), _p(stash), _p(ws), wsf, B, T, I, H, s)
     assert rc == 0, _lib.last_error()
-    grads = {k: torch.empty(*shape, device=dev) for k, shape in dict(
+    grads = {k: buf(*shape) for k, shape in dict(
         dx=(B, T, I), dh0=(B, H), dw_ih=(3 * H, I), dw_hh=(3 * H, H), db_ih=(3 * H,), db_hh=(3 * H,)).items()}
     wsb = lib.gru_backward_workspace_bytes(B, T, I, H)
     ws2 = torch.empty(wsb, dtype=torch.uint8, device=dev)
@@ -70,6 +80,23 @@ def test_capi_forward_backward_vs_oracle(B, T, I, H, with_dout):
         np.testing.assert_allclose(st_gpu[:, :, i], st[k], rtol=RTOL, atol=ATOL, err_msg=k)
     for k in grads:
         np.testing.assert_allclose(grads[k].cpu().numpy(), g[k], rtol=RTOL, atol=ATOL, err_msg=k)
+
+
+@pytest.mark.parametrize("B,T,I,H", [(3, 7, 5, 33), (4, 16, 64, 256), (2, 5, 3, 129), (17, 4, 2, 20)])
+@pytest.mark.parametrize("with_dout", [True, False])
+def test_capi_forward_backward_vs_oracle(B, T, I, H, with_dout):
+    _run_capi(B, T, I, H, with_dout)
+
+
+@pytest.mark.parametrize("B,T,I,H", [(4, 9, 32, 64), (3, 6, 8, 256), (2, 5, 12, 128)])
+def test_capi_unaligned_caller_buffers(B, T, I, H):
+    # every caller pointer 4 bytes past a 16-byte boundary
+    _run_capi(B, T, I, H, True, offset=1)
+
+
+def test_capi_long_sequence():
+    # many passes through the input ring and both mbarrier phases
+    _run_capi(3, 2500, 16, 130, True, seed=2500)
 
 
 def test_capi_inference_without_stash():
