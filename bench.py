@@ -48,6 +48,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cudnn", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="eager steps only (no CUDA graph replay)")
     return ap.parse_args()
 
 
@@ -223,7 +224,7 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
 
-    from rnn_kernel_b200 import GRU, DataParallelTrainer, _lib
+    from rnn_kernel_b200 import GRU, DataParallelTrainer, GraphedTrainStep, _lib
 
     B = args.global_batch // world if args.global_batch else args.batch_per_gpu
     T, I, H, L = args.seq_len, args.input_size, args.hidden_size, args.layers
@@ -249,26 +250,55 @@ def main():
         trainer.step(x, y)
     torch.cuda.synchronize()
 
-    # ---- timed region (device-resident inputs) ----
+    def mean_median_max(times):
+        m = sum(times) / len(times)
+        srt = sorted(times)
+        n = len(srt)
+        md = srt[n // 2] if n % 2 else 0.5 * (srt[n // 2 - 1] + srt[n // 2])
+        if world > 1:
+            t = torch.tensor([m, md], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            m, md = float(t[0]), float(t[1])
+        return m, md
+
+    # ---- eager pass: per-kernel device times (library telemetry) ----
     barrier()
     torch.cuda.synchronize()
     _lib.timing_enable(True)
     _lib.timing_collect()
     launches0 = _lib.launch_count()
-    with ClockSampler(local) as clk:
-        times = timed_steps(lambda k: trainer.step(x, y), K, flush, torch)
-    launches = _lib.launch_count() - launches0
+    etimes = timed_steps(lambda k: trainer.step(x, y), K, flush, torch)
+    launches_eager = _lib.launch_count() - launches0
     _lib.timing_enable(False)
     ktimes = _lib.timing_collect()
     torch.cuda.synchronize()
     barrier()
-    ms = sum(times) / K
-    med = sorted(times)[K // 2] if K % 2 else 0.5 * (sorted(times)[K // 2 - 1] + sorted(times)[K // 2])
-    if world > 1:
-        t = torch.tensor([ms, med], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, med = float(t[0]), float(t[1])
+    eager_ms, eager_med = mean_median_max(etimes)
+
+    # ---- headline: the same step replayed from a CUDA graph ----
+    # (zero grads + fwd + loss + bwd captured; all-reduce and SGD eager).
+    # Library kernels per replay = launches during capture.
+    graph, graph_error, per_step_lib = None, None, 0
+    if not args.no_graph:
+        try:
+            n0 = _lib.launch_count()
+            graph = GraphedTrainStep(trainer, [(x, y)], warmup=3)
+            per_step_lib = (_lib.launch_count() - n0) - 3 * (launches_eager // K)
+        except Exception as exc:  # capture unavailable: eager headline
+            graph = None
+            graph_error = f"{type(exc).__name__}: {exc}"[:200]
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        if graph is not None:
+            times = timed_steps(lambda k: graph.step(0), K, flush, torch)
+        else:
+            times = timed_steps(lambda k: trainer.step(x, y), K, flush, torch)
+    torch.cuda.synchronize()
+    barrier()
     clocks = clk.summary()
+    ms, med = mean_median_max(times)
+    launches = per_step_lib * K if graph is not None else launches_eager
     value = B * world * T / (ms / 1e3)
 
     # ---- end to end through the public API from pinned host buffers ----
@@ -285,18 +315,36 @@ def main():
         yh = y.cpu().pin_memory()
         lh = torch.empty(1, pin_memory=True)
 
+        # With the graph, each step replays the capture whose static inputs
+        # are the buffers the batch was copied into.
         def e2e_serial_step(k):
-            xd = xh.to(dev, non_blocking=True)
-            yd = yh.to(dev, non_blocking=True)
-            loss = trainer.step(xd, yd)
+            if graph is not None:
+                x.copy_(xh, non_blocking=True)
+                y.copy_(yh, non_blocking=True)
+                loss = graph.step(0)
+            else:
+                xd = xh.to(dev, non_blocking=True)
+                yd = yh.to(dev, non_blocking=True)
+                loss = trainer.step(xd, yd)
             lh.copy_(loss.reshape(1), non_blocking=True)
 
         pf = HostBatchPrefetcher(dev)
+        pgraph = None
+        if graph is not None:
+            # allocate both buffer sets, then capture one graph on each
+            for _ in range(2):
+                pf.put(xh, yh)
+                pf.get()
+            torch.cuda.synchronize()
+            pgraph = GraphedTrainStep(trainer, [pf._bufs[0], pf._bufs[1]], warmup=1)
+            torch.cuda.synchronize()
+        pf.put(xh, yh)  # one batch ahead from here on
 
         def e2e_step(k):
             xd, yd = pf.get()
-            pf.put(xh, yh)  # the next step's batch, overlapped with this step
-            loss = trainer.step(xd, yd)
+            slot = pf._in_use
+            pf.put(xh, yh)  # the next step's batch, into the other set, overlapped with this step
+            loss = pgraph.step(slot) if pgraph is not None else trainer.step(xd, yd)
             lh.copy_(loss.reshape(1), non_blocking=True)
 
         def timed_e2e(fn):
@@ -313,9 +361,9 @@ def main():
             return ems
 
         serial_ms = timed_e2e(e2e_serial_step)
-        pf.put(xh, yh)
         ems = timed_e2e(e2e_step)
-        pf.get()  # drain the last prefetch
+        while pf._queue:  # drain the outstanding prefetch
+            pf.get()
         torch.cuda.synchronize()
         e2e = {"value": B * world * T / (ems / 1e3), "unit": UNIT, "ms_per_step": ems,
                "h2d_bytes_per_step": (x.numel() + y.numel()) * 4, "d2h_bytes_per_step": 4,
@@ -369,7 +417,8 @@ def main():
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
-        "ms_per_step": ms, "median_ms_per_step": med, "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
+        "ms_per_step": ms, "median_ms_per_step": med, "higher_is_better": True,
+        "graph": graph is not None, "eager_ms_per_step": eager_ms, "eager_median_ms_per_step": eager_med, "scaling": scaling, "vs_baseline": None,
         "dtype": "fp32", "data": "synthetic: x, target ~ N(0,1) per rank (seed 1000+rank); weights U(-1/16,1/16)",
         "config": {"workload": f"gru_train_step 1-layer I={I} H={H} T={T}, batch {B}/GPU "
                                f"(fwd + MSE + bwd + allreduce + SGD lr 1e-2)",
@@ -383,6 +432,8 @@ def main():
         "e2e": e2e,
         "impl": "b200",
     }
+    if graph_error:
+        line["graph_error"] = graph_error
 
     if world == 1 and not args.no_cudnn:
         from torch import nn

@@ -12,7 +12,7 @@ from .gru import (
     is_b200_available,
     is_supported_gru,
 )
-from .train import DataParallelTrainer, HostBatchPrefetcher, flatten_parameters_
+from .train import DataParallelTrainer, GraphedTrainStep, HostBatchPrefetcher, flatten_parameters_
 
 B200GRU = GRU
 
@@ -22,6 +22,7 @@ __all__ = [
     "GRUFunction",
     "MAX_HIDDEN_SIZE",
     "DataParallelTrainer",
+    "GraphedTrainStep",
     "HostBatchPrefetcher",
     "flatten_parameters_",
     "from_torch_gru",

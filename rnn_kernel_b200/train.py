@@ -111,6 +111,13 @@ class DataParallelTrainer:
 
     def step(self, x: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
         """One train step on this rank's shard; returns the shard loss (detached)."""
+        loss = self.forward_backward(x, target)
+        self.reduce_and_update()
+        return loss
+
+    def forward_backward(self, x: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
+        """Zero the gradients, forward, loss and backward (the per-layer
+        all-reduces start here when bucket overlap is on)."""
         self.grad.zero_()
         if self._buckets:
             self._pending = [n for _, _, n in self._buckets]
@@ -121,6 +128,10 @@ class DataParallelTrainer:
             loss.backward()
         finally:
             self._in_step = False
+        return loss.detach()
+
+    def reduce_and_update(self) -> None:
+        """Finish the gradient all-reduce and apply the SGD update."""
         if self.world > 1 and self._buckets:
             for w in self._works:
                 w.wait()
@@ -133,7 +144,48 @@ class DataParallelTrainer:
             dist.all_reduce(self.grad, op=dist.ReduceOp.SUM, group=self.group)
         with torch.no_grad():
             self.flat.add_(self.grad, alpha=-self.lr / self.world)
-        return loss.detach()
+
+
+class GraphedTrainStep:
+    """A :class:`DataParallelTrainer` step replayed from CUDA graphs.
+
+    The device work of zeroing the gradients, the forward, the loss and the
+    backward (this library's kernels and torch's) is captured once per static
+    input pair and replayed with one launch; the gradient all-reduce and the
+    SGD update run eagerly after each replay, so no collective is captured.
+    ``inputs`` lists the static ``(x, target)`` device tensor pairs (for
+    instance the two buffer sets of a :class:`HostBatchPrefetcher`);
+    ``step(i)`` replays graph ``i`` on whatever those tensors hold now.
+    Per-layer bucket overlap is switched off (the all-reduce follows the
+    replay).  Capture warms up on a side stream first (``warmup`` steps per
+    input pair), as CUDA graph capture requires; those warm-up steps train
+    like any other step.
+    """
+
+    def __init__(self, trainer: DataParallelTrainer, inputs, warmup: int = 3) -> None:
+        self.trainer = trainer
+        trainer._buckets = []
+        self.inputs = list(inputs)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                for x, y in self.inputs:
+                    trainer.step(x, y)
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        self.graphs, self.losses = [], []
+        for x, y in self.inputs:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                loss = trainer.forward_backward(x, y)
+            self.graphs.append(g)
+            self.losses.append(loss)
+
+    def step(self, i: int = 0) -> torch.Tensor:
+        self.graphs[i].replay()
+        self.trainer.reduce_and_update()
+        return self.losses[i]
 
 
 class HostBatchPrefetcher:

@@ -66,3 +66,68 @@ def test_training_through_prefetcher_matches_device_inputs():
     l2, w2 = run(False)
     assert l1 == l2
     assert torch.equal(w1, w2)
+
+
+def test_graphed_steps_match_eager_steps():
+    from rnn_kernel_b200 import GraphedTrainStep
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator().manual_seed(3)
+    host = [(torch.randn(5, 11, 24, generator=g), torch.randn(5, 11, 40, generator=g)) for _ in range(6)]
+
+    def make():
+        torch.manual_seed(21)
+        return DataParallelTrainer(GRU(24, 40, num_layers=2).to(dev), lr=1e-2)
+
+    # eager reference: 3 warm-up steps on batch 0 (what the capture warm-up
+    # does), then one step per batch
+    ref = make()
+    x0, y0 = (t.to(dev) for t in host[0])
+    for _ in range(3):
+        ref.step(x0, y0)
+    ref_losses = [float(ref.step(x.to(dev), y.to(dev))) for x, y in host]
+
+    tr = make()
+    xs, ys = x0.clone(), y0.clone()
+    gs = GraphedTrainStep(tr, [(xs, ys)], warmup=3)
+    losses = []
+    for x, y in host:
+        xs.copy_(x)
+        ys.copy_(y)
+        losses.append(float(gs.step(0)))
+    assert losses == ref_losses
+    assert torch.equal(tr.flat, ref.flat)
+
+
+def test_graphed_steps_on_prefetcher_buffers():
+    from rnn_kernel_b200 import GraphedTrainStep
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator().manual_seed(4)
+    host = [(torch.randn(3, 7, 16, generator=g).pin_memory(), torch.randn(3, 7, 32, generator=g).pin_memory())
+            for _ in range(5)]
+    torch.manual_seed(5)
+    ref = DataParallelTrainer(GRU(16, 32).to(dev), lr=1e-2)
+    torch.manual_seed(5)
+    tr = DataParallelTrainer(GRU(16, 32).to(dev), lr=1e-2)
+
+    pf = HostBatchPrefetcher(dev)
+    for _ in range(2):  # allocate both buffer sets with batch 0
+        pf.put(*host[0])
+        pf.get()
+    torch.cuda.synchronize()
+    gs = GraphedTrainStep(tr, [pf._bufs[0], pf._bufs[1]], warmup=1)
+    x0, y0 = (t.to(dev) for t in host[0])
+    for _ in range(2):  # the capture warm-up: one step per buffer set, batch 0
+        ref.step(x0, y0)
+    pf.put(*host[0])
+    losses, ref_losses = [], []
+    for k in range(len(host)):
+        pf.get()
+        slot = pf._in_use
+        if k + 1 < len(host):
+            pf.put(*host[k + 1])
+        losses.append(float(gs.step(slot)))
+        ref_losses.append(float(ref.step(host[k][0].to(dev), host[k][1].to(dev))))
+    assert losses == ref_losses
+    assert torch.equal(tr.flat, ref.flat)
