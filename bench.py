@@ -197,6 +197,10 @@ def load_traffic():
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
+# Graph replay with more than one rank (all-reduce stays eager either way).
+GRAPH_MULTI_GPU = False
+
+
 def timed_steps(step_fn, K, flush, torch):
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     for k in range(K):
@@ -279,10 +283,11 @@ def main():
     # (zero grads + fwd + loss + bwd captured; all-reduce and SGD eager).
     # Library kernels per replay = launches during capture.
     graph, graph_error, per_step_lib = None, None, 0
-    if not args.no_graph:
+    cmode = "thread_local" if world > 1 else "global"
+    if not args.no_graph and not (world > 1 and not GRAPH_MULTI_GPU):
         try:
             n0 = _lib.launch_count()
-            graph = GraphedTrainStep(trainer, [(x, y)], warmup=3)
+            graph = GraphedTrainStep(trainer, [(x, y)], warmup=3, capture_error_mode=cmode)
             per_step_lib = (_lib.launch_count() - n0) - 3 * (launches_eager // K)
         except Exception as exc:  # capture unavailable: eager headline
             graph = None
@@ -336,7 +341,7 @@ def main():
                 pf.put(xh, yh)
                 pf.get()
             torch.cuda.synchronize()
-            pgraph = GraphedTrainStep(trainer, [pf._bufs[0], pf._bufs[1]], warmup=1)
+            pgraph = GraphedTrainStep(trainer, [pf._bufs[0], pf._bufs[1]], warmup=1, capture_error_mode=cmode)
             torch.cuda.synchronize()
         pf.put(xh, yh)  # one batch ahead from here on
 

@@ -159,10 +159,13 @@ class GraphedTrainStep:
     Per-layer bucket overlap is switched off (the all-reduce follows the
     replay).  Capture warms up on a side stream first (``warmup`` steps per
     input pair), as CUDA graph capture requires; those warm-up steps train
-    like any other step.
+    like any other step.  ``capture_error_mode`` is passed to
+    ``torch.cuda.graph``; with a process group, "thread_local" keeps other
+    threads (NCCL's watchdog) free to query CUDA while this one captures.
     """
 
-    def __init__(self, trainer: DataParallelTrainer, inputs, warmup: int = 3) -> None:
+    def __init__(self, trainer: DataParallelTrainer, inputs, warmup: int = 3,
+                 capture_error_mode: str = "global") -> None:
         self.trainer = trainer
         trainer._buckets = []
         self.inputs = list(inputs)
@@ -177,7 +180,7 @@ class GraphedTrainStep:
         self.graphs, self.losses = [], []
         for x, y in self.inputs:
             g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
+            with torch.cuda.graph(g, capture_error_mode=capture_error_mode):
                 loss = trainer.forward_backward(x, y)
             self.graphs.append(g)
             self.losses.append(loss)
