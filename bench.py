@@ -80,6 +80,15 @@ class ClockSampler:
                  "-lms", "50"], stdout=self.tmp, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return self
+        # nvidia-smi takes a moment to start: wait (bounded) for its first
+        # sample so that sampling is live when the timed region begins
+        t0 = time.time()
+        while time.time() - t0 < 5.0 and self.proc.poll() is None:
+            self.tmp.flush()
+            if os.path.getsize(self.tmp.name) > 0:
+                break
+            time.sleep(0.02)
         return self
 
     def __exit__(self, *exc):
@@ -198,7 +207,7 @@ def load_traffic():
 # our arm
 # ---------------------------------------------------------------------------
 # Graph replay with more than one rank (all-reduce stays eager either way).
-GRAPH_MULTI_GPU = False
+GRAPH_MULTI_GPU = True
 
 
 def timed_steps(step_fn, K, flush, torch):
