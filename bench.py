@@ -1,11 +1,11 @@
 #!/usr/bin/env python
-"""GRU FP32 train-step benchmark (BASELINE metric: samples*timesteps/s).
+"""GRU FP32 train-step benchmark (samples*timesteps/s).
 
 One step = forward + MSE loss + backward + (all-reduce for N > 1) + SGD
-lr 1e-2 of a 1-layer GRU, I = H = 256, T = 512, batch 64 per GPU (BASELINE
-config 2 at N = 1; weak scaling at N > 1, i.e. config 5's DP step with
-64 rows per rank).  ``--global-batch`` switches to config 5's strong-scaling
-form (global batch split evenly over the ranks).
+lr 1e-2 of a 1-layer GRU, I = H = 256, T = 512, batch 64 per GPU (the
+reference's production a100_gru_h256 shape at N = 1; weak scaling at N > 1:
+the data-parallel step with 64 rows per rank).  ``--global-batch`` switches
+the headline to strong scaling (a global batch split evenly over the ranks).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
     python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N

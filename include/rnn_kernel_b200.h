@@ -93,7 +93,9 @@ int gru_backward(const float* dout, const float* dhn, const float* x, const floa
  * array's device address (once per device, with that device current); make
  * that first call before any stream capture.  All calls on a device share the
  * one array, so calls that overlap on the GPU (different streams, no ordering
- * between them) race; serialise them. */
+ * between them) race; serialise them.  The looked-up address is cached per
+ * device ordinal for the process's life: resetting the device or recreating
+ * its primary context while the library is loaded is not supported. */
 int gru_forward_inference_noalloc(const float* x, const float* h0, const float* w_ih,
                                   const float* w_hh, const float* b_ih, const float* b_hh,
                                   float* out, float* hn, int B, int T, int I, int H, void* stream);

@@ -4,7 +4,7 @@ The reference's own CPU path for this workload is stock ``torch.nn.GRU``
 driven by its harness (``rnn_benchmark.py --device cpu``: model built at
 ``rnn_benchmark.py:198-207``, ``train_step`` at ``:628-639``, tokens/s =
 B*T*steps/s at ``:754``).  This module times exactly that on the host cores
-with the BASELINE loss/optimizer (MSE against an N(0,1) target, SGD lr 1e-2),
+with the benchmark's loss/optimizer (MSE against an N(0,1) target, SGD lr 1e-2),
 all threads, ``time.perf_counter`` around each step.
 """
 from __future__ import annotations

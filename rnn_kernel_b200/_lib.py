@@ -12,6 +12,12 @@ from pathlib import Path
 
 from . import build as _build
 
+# status codes of include/rnn_kernel_b200.h
+GRU_OK = 0
+GRU_ERR_INVALID = 1
+GRU_ERR_CUDA = 2
+GRU_ERR_UNSUPPORTED = 3
+
 _lock = threading.Lock()
 _lib = None
 

@@ -6,11 +6,16 @@
 // cudaMalloc there would fragment or exceed a budget the host enforces), and
 // code running where an allocation would stall or is not allowed.  For them
 // this entry point runs the same forward as gru_forward(stash = NULL), but its
-// scratch (the input-gate buffer and, when input_size is not a multiple of 4,
-// the 16-byte-stride copies of x and W_ih) lives in one file-scope device
-// array of GRU_NOALLOC_SCRATCH_BYTES that is part of the loaded module: every
-// GPU that loads the library holds it until the process exits.  Nothing here
-// calls cudaMalloc, cudaFree or an allocating library routine.
+// scratch (always the input-gate buffer plus the TF32 hi/lo split copies of x
+// and W_ih that feed the tensor-core projection) lives in one file-scope
+// device array of GRU_NOALLOC_SCRATCH_BYTES that is part of the loaded module:
+// every GPU that loads the library holds it until the process exits.  Nothing
+// here calls cudaMalloc, cudaFree or an allocating library routine.
+//
+// The array's device address is looked up once per device ordinal and cached
+// for the life of the process.  Resetting a device (cudaDeviceReset) or
+// otherwise tearing down and recreating its primary context while the library
+// stays loaded is not supported: the cached address would be stale.
 
 #include <cuda_runtime.h>
 

@@ -1,8 +1,8 @@
 """Data-parallel GRU training over one process per GPU (NCCL over NVLink).
 
-The reference has no distributed code; this is the B200 build's DP layer for
-BASELINE config 5 (global batch sharded evenly across 1/2/4/8 GPUs, MSE per
-shard, gradients all-reduced, SGD).
+The reference has no distributed code; this is the B200 build's DP layer:
+the global batch is sharded evenly across 1/2/4/8 GPUs, each rank takes the
+MSE of its shard, gradients are all-reduced and SGD updates every replica.
 
 Design: all parameters of the model are re-pointed into ONE flat FP32 buffer
 and their ``.grad`` into ONE flat gradient buffer.  Autograd accumulates each
@@ -66,6 +66,10 @@ class DataParallelTrainer:
         self._pending: list = []   # parameters of each bucket not yet accumulated this step
         self._works: list = []
         self._in_step = False
+        # Per-layer overlapped all-reduce; switched off (hooks stay registered
+        # but return at once) by GraphedTrainStep, whose replay is followed by
+        # one all-reduce of the whole buffer.
+        self.overlap_active = False
         if self.world > 1:
             # Every rank starts from rank 0's weights.
             dist.broadcast(self.flat, src=0, group=process_group)
@@ -95,10 +99,11 @@ class DataParallelTrainer:
             for p in ps:
                 p.register_post_accumulate_grad_hook(lambda _p, b=b: self._param_ready(b))
         self._pending = [n for _, _, n in self._buckets]
+        self.overlap_active = True
 
     def _param_ready(self, b: int) -> None:
-        if not self._in_step:
-            return  # a backward outside step(): leave the gradients alone
+        if not self._in_step or not self.overlap_active:
+            return  # a backward outside step(), or overlap off: leave the gradients alone
         self._pending[b] -= 1
         if self._pending[b] == 0:
             lo, hi, _ = self._buckets[b]
@@ -119,7 +124,7 @@ class DataParallelTrainer:
         """Zero the gradients, forward, loss and backward (the per-layer
         all-reduces start here when bucket overlap is on)."""
         self.grad.zero_()
-        if self._buckets:
+        if self.overlap_active:
             self._pending = [n for _, _, n in self._buckets]
             self._works = []
         loss = self.loss(x, target)
@@ -132,7 +137,7 @@ class DataParallelTrainer:
 
     def reduce_and_update(self) -> None:
         """Finish the gradient all-reduce and apply the SGD update."""
-        if self.world > 1 and self._buckets:
+        if self.world > 1 and self.overlap_active:
             for w in self._works:
                 w.wait()
             # a layer whose parameters got no gradient this step
@@ -156,8 +161,9 @@ class GraphedTrainStep:
     ``inputs`` lists the static ``(x, target)`` device tensor pairs (for
     instance the two buffer sets of a :class:`HostBatchPrefetcher`);
     ``step(i)`` replays graph ``i`` on whatever those tensors hold now.
-    Per-layer bucket overlap is switched off (the all-reduce follows the
-    replay).  Capture warms up on a side stream first (``warmup`` steps per
+    Per-layer bucket overlap is switched off for the trainer (its hooks
+    stay registered but do nothing; the all-reduce of the whole buffer
+    follows the replay); ``close()`` switches it back on.  Capture warms up on a side stream first (``warmup`` steps per
     input pair), as CUDA graph capture requires; those warm-up steps train
     like any other step.  ``capture_error_mode`` is passed to
     ``torch.cuda.graph``; with a process group, "thread_local" keeps other
@@ -167,7 +173,9 @@ class GraphedTrainStep:
     def __init__(self, trainer: DataParallelTrainer, inputs, warmup: int = 3,
                  capture_error_mode: str = "global") -> None:
         self.trainer = trainer
-        trainer._buckets = []
+        trainer.overlap_active = False
+        trainer._pending = [n for _, _, n in trainer._buckets]
+        trainer._works = []
         self.inputs = list(inputs)
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
@@ -189,6 +197,11 @@ class GraphedTrainStep:
         self.graphs[i].replay()
         self.trainer.reduce_and_update()
         return self.losses[i]
+
+    def close(self) -> None:
+        """Drop the graphs and give the trainer its per-layer overlap back."""
+        self.graphs, self.losses = [], []
+        self.trainer.overlap_active = bool(self.trainer._buckets) and self.trainer.world > 1
 
 
 class HostBatchPrefetcher:

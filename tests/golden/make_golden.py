@@ -8,7 +8,7 @@ the same seeded inputs, and stores inputs, outputs and every gradient.
 
 Cases mirror the reference's own parity tests:
 
-* ``smoke``       - the BASELINE config-1 quick check (I=H=16, B=2, T=8, seed 0,
+* ``smoke``       - the quick-check shape (I=H=16, B=2, T=8, seed 0,
                     h0=0, MSE against an N(0,1) target);
 * ``h7_l2``       - ``tests/test_custom_gru.py:17-22`` (seed 321, I=4, H=7, L=2,
                     B=3, T=5, random h0, random grad_out / grad_h);

@@ -1,6 +1,6 @@
 """Data-parallel trainer logic on CPU gloo ranks (world_size 2).
 
-BASELINE config 5's check, scaled down: global batch sharded evenly, rank r
+The data-parallel equivalence check, scaled down: global batch sharded evenly, rank r
 draws its shard from seed+r, MSE per shard, all-reduced gradients, SGD lr
 1e-2; after 10 steps loss and weights match a single-process run over the
 concatenated batch.  torch.nn.GRU stands in for the per-rank compute (the DP
@@ -40,9 +40,14 @@ def _worker(rank, world, port, out_path, layers=1, overlap=True):
     torch.manual_seed(0 if rank == 0 else 99)  # weights differ until the broadcast
     model = torch.nn.GRU(I, H, num_layers=layers, batch_first=True)
     tr = DataParallelTrainer(model, lr=LR, overlap=overlap)
-    assert bool(tr._buckets) == (overlap and layers > 1)
+    assert bool(tr._buckets) == (bool(overlap) and layers > 1)
     losses = []
     for step in range(STEPS):
+        if overlap == "toggle":
+            # what GraphedTrainStep does to the trainer, every other step: the
+            # per-layer hooks stay registered but the whole buffer is reduced
+            # after the backward (used to raise IndexError from the hooks)
+            tr.overlap_active = step % 2 == 1
         x, y = _shard(rank, step, GLOBAL_B // world)
         loss = tr.step(x, y)
         t = loss.clone()
@@ -78,7 +83,7 @@ def test_flatten_parameters_views():
 
 
 @pytest.mark.timeout(300)
-@pytest.mark.parametrize("layers,overlap", [(1, True), (2, True), (2, False)])
+@pytest.mark.parametrize("layers,overlap", [(1, True), (2, True), (2, False), (2, "toggle")])
 def test_dp_gloo_two_ranks_matches_single_process(layers, overlap):
     # layers=2, overlap=True: per-layer buckets all-reduced asynchronously
     # from post-accumulate-grad hooks while the lower layer's backward runs.

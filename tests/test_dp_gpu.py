@@ -1,5 +1,4 @@
-"""Data-parallel training on 2 GPUs with NCCL (BASELINE config 5's check,
-scaled down): the global batch is sharded evenly, rank r draws its shard from
+"""Data-parallel training on 2 GPUs with NCCL (scaled down): the global batch is sharded evenly, rank r draws its shard from
 seed + r, each rank runs the B200 GRU on its own GPU, gradients are
 all-reduced, SGD lr 1e-2; after 10 steps the loss and the weights match a
 single-process run over the concatenated batch.  Skipped with fewer than 2

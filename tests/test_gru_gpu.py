@@ -48,7 +48,7 @@ def test_small_shapes(I, H, L, B, T):
 
 @pytest.mark.parametrize("H", [64, 96, 128, 129, 130, 160, 192, 256])
 def test_hidden_sweep_config3(H):
-    # input_size=H, batch=64, seq_len=256, seed = H, MSE loss.
+    # Hidden-size sweep: input_size=H, batch=64, seq_len=256, seed = H, MSE loss.
     mine, theirs, truth = run_pair(H, H, 1, 64, 256, seed=H, loss="mse", h0_scale=0)
     assert_parity(mine, theirs, truth)
 
@@ -61,7 +61,7 @@ def test_hidden_sweep_unit_grads(H):
 
 
 def test_prod_shape_config2():
-    # I=H=256, B=64, T=512, h0=0, MSE against N(0,1) target.
+    # Production shape: I=H=256, B=64, T=512, h0=0, MSE against N(0,1) target.
     mine, theirs, truth = run_pair(256, 256, 1, 64, 512, seed=2, loss="mse", h0_scale=0)
     assert_parity(mine, theirs, truth)
 
@@ -73,7 +73,7 @@ def test_prod_shape_random_grads():
 
 
 def test_stacked_config4():
-    # 2 layers, I=128, H=256, B=128, T=1024, h0 ~ 0.1*N(0,1), loss sum(out^2).
+    # Stacked: 2 layers, I=128, H=256, B=128, T=1024, h0 ~ 0.1*N(0,1), loss sum(out^2).
     mine, theirs, truth = run_pair(128, 256, 2, 128, 1024, seed=4, loss="sumsq", h0_scale=0.1)
     # d(sum out^2)/d out = 2*out is unit-scale: weight gradients use the envelope check.
     assert_parity(mine, theirs, truth, weights="envelope")

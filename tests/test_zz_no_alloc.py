@@ -77,5 +77,5 @@ def test_noalloc_rejects_shapes_beyond_its_scratch():
     rc = lib.gru_forward_inference_noalloc(_p(c["x"]), _p(c["h0"]), _p(c["w_ih"]), _p(c["w_hh"]), _p(c["b_ih"]),
                                            _p(c["b_hh"]), _p(out), _p(out), B, T, I, H,
                                            torch.cuda.current_stream().cuda_stream)
-    assert rc == 3
+    assert rc == _lib.GRU_ERR_UNSUPPORTED
     assert "scratch" in _lib.last_error()
