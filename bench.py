@@ -7,13 +7,24 @@ reference's production a100_gru_h256 shape at N = 1; weak scaling at N > 1:
 the data-parallel step with 64 rows per rank).  ``--global-batch`` switches
 the headline to strong scaling (a global batch split evenly over the ranks).
 
+Beside the headline the line carries
+* ``strong``: the data-parallel workload with a global batch of 1024 split
+  evenly over the N ranks (I = H = 256, T = 512), timed the same way;
+* ``dp_check`` (N > 1): 10 data-parallel steps on that workload (rank r
+  draws its shard from seed + r) against one GPU running the concatenated
+  batch from the same initial weights: loss and weights must agree;
+* ``cudnn_sweep`` (N = 1): this library vs cuDNN ``torch.nn.GRU`` on the
+  same GPU over hidden sizes 64..256 (I = H, B = 64, T = 256), the stacked
+  2-layer shape (I = 128, H = 256, B = 128, T = 1024, loss sum(out^2),
+  random h0) and the B = 1024 batch.
+
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
     python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N
 
 Rank 0 prints one JSON line.  Timing: W untimed warm-up steps, then exactly K
 steps, each bracketed by CUDA events on the launching stream, with a 256 MiB
 L2 flush between steps outside the events; barrier + synchronize on both
-sides; the per-step time is the max over ranks.
+sides; per-step statistics are the max over ranks.
 """
 from __future__ import annotations
 
@@ -22,7 +33,7 @@ import json
 import os
 import subprocess
 import sys
-import tempfile
+import threading
 import time
 from pathlib import Path
 
@@ -31,6 +42,7 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "GRU fp32 train samples·timesteps/s at H=256, 1/2/4/8 B200 vs cuDNN & host CPU"
 UNIT = "samples*timesteps/s"
+STRONG_GLOBAL_BATCH = 1024
 
 
 def parse():
@@ -48,6 +60,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cudnn", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-strong", action="store_true", help="skip the global-batch-1024 sub-measurement")
+    ap.add_argument("--no-dp-check", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the cuDNN comparison sweep")
     ap.add_argument("--no-graph", action="store_true", help="eager steps only (no CUDA graph replay)")
     return ap.parse_args()
 
@@ -60,72 +75,111 @@ def dist_env():
 
 
 # ---------------------------------------------------------------------------
-# clocks: nvidia-smi sampled during the timed region
+# clocks sampled during the timed region
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock, power and throttle reasons of one GPU, sampled every few ms
+    through NVML on a thread (nvidia-smi's polling is too coarse for a timed
+    region of tens of milliseconds); one nvidia-smi reading when NVML is
+    unavailable.  Reads settings only; changes nothing."""
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.tmp = None
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, cuda_index: int, period_s: float = 0.002):
+        self.cuda_index = cuda_index
+        self.period = period_s
+        self.rows = []  # (sm_mhz, max_mhz, power_w, [reason flags])
+        self.error = None
+        self._stop = threading.Event()
+        self._thr = None
+        self._nv = None
+        self._h = None
+
+    def _handle(self):
+        import pynvml as nv
+
+        nv.nvmlInit()
+        self._nv = nv
+        try:
+            import torch
+
+            uuid = str(torch.cuda.get_device_properties(self.cuda_index).uuid)
+            return nv.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(self.cuda_index)
+
+    def _sample(self):
+        nv, h = self._nv, self._h
+        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+        rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        flags = [bool(rs & nv.nvmlClocksEventReasonHwSlowdown),
+                 bool(rs & nv.nvmlClocksEventReasonHwThermalSlowdown),
+                 bool(rs & nv.nvmlClocksEventReasonSwThermalSlowdown),
+                 bool(rs & nv.nvmlClocksEventReasonSwPowerCap)]
+        self.rows.append((float(sm), float(mx), pw, flags))
+
+    def _loop(self):
+        while not self._stop.is_set():
+            try:
+                self._sample()
+            except Exception as exc:  # pragma: no cover - depends on the driver
+                self.error = f"{type(exc).__name__}: {exc}"
+                return
+            time.sleep(self.period)
 
     def __enter__(self):
         try:
-            self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "50"], stdout=self.tmp, stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            self._h = self._handle()
+            self._sample()  # live before the timed region starts
+        except Exception as exc:
+            self._h = None
+            self.error = f"NVML unavailable: {type(exc).__name__}: {exc}"
             return self
-        # nvidia-smi takes a moment to start: wait (bounded) for its first
-        # sample so that sampling is live when the timed region begins
-        t0 = time.time()
-        while time.time() - t0 < 5.0 and self.proc.poll() is None:
-            self.tmp.flush()
-            if os.path.getsize(self.tmp.name) > 0:
-                break
-            time.sleep(0.02)
+        self._thr = threading.Thread(target=self._loop, daemon=True)
+        self._thr.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self._stop.set()
+        if self._thr is not None:
+            self._thr.join(timeout=5)
+        if self._h is None:
+            self.rows = nvidia_smi_sample(self.cuda_index)
 
     def summary(self):
-        if self.proc is None or self.tmp is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        rows = []
-        with open(self.tmp.name) as f:
-            for line in f:
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) < 9:
-                    continue
-                try:
-                    rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[4:]))
-                except ValueError:
-                    continue
-        os.unlink(self.tmp.name)
+        rows = self.rows
         if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "error": self.error}
         load = [r for r in rows if r[2] > 200.0] or rows
         sm = sorted(r[0] for r in load)
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = set()
-        for r in load:
-            for name, v in zip(names, r[3][1:]):
-                if v.lower().startswith("active"):
-                    reasons.add(name)
-        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": sorted(reasons), "samples": len(load),
-                "power_w_max": max(r[2] for r in rows)}
+        reasons = sorted({n for r in load for n, f in zip(self.NAMES, r[3]) if f})
+        out = {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+               "samples": len(load), "power_w_max": max(r[2] for r in rows),
+               "source": "nvml" if self._h is not None else "nvidia-smi"}
+        if self.error:
+            out["error"] = self.error
+        return out
+
+
+def nvidia_smi_sample(gpu: int):
+    q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+    try:
+        out = subprocess.run(["nvidia-smi", "-i", str(gpu), f"--query-gpu={q}", "--format=csv,noheader,nounits"],
+                             capture_output=True, text=True, timeout=20).stdout
+    except (OSError, subprocess.SubprocessError):
+        return []
+    rows = []
+    for line in out.splitlines():
+        p = [x.strip() for x in line.split(",")]
+        try:
+            rows.append((float(p[0]), float(p[1]), float(p[2]), [v.lower().startswith("active") for v in p[3:7]]))
+        except (ValueError, IndexError):
+            continue
+    return rows
 
 
 # ---------------------------------------------------------------------------
@@ -204,12 +258,8 @@ def load_traffic():
 
 
 # ---------------------------------------------------------------------------
-# our arm
+# timing helpers
 # ---------------------------------------------------------------------------
-# Graph replay with more than one rank (all-reduce stays eager either way).
-GRAPH_MULTI_GPU = True
-
-
 def timed_steps(step_fn, K, flush, torch):
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     for k in range(K):
@@ -221,6 +271,164 @@ def timed_steps(step_fn, K, flush, torch):
     return [a.elapsed_time(b) for a, b in evs]
 
 
+def step_stats(times, world, dev, torch, dist):
+    """mean / p50 / p90 / max of per-step ms, each the max over ranks."""
+    srt = sorted(times)
+    n = len(srt)
+
+    def pct(q):
+        return srt[min(n - 1, max(0, int(round(q * (n - 1)))))]
+
+    v = [sum(times) / n, pct(0.5), pct(0.9), srt[-1]]
+    if world > 1:
+        t = torch.tensor(v, device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        v = [float(x) for x in t]
+    return {"mean": v[0], "p50": v[1], "p90": v[2], "max": v[3]}
+
+
+# ---------------------------------------------------------------------------
+# sub-measurements
+# ---------------------------------------------------------------------------
+def strong_scaling(args, world, rank, dev, K, W, flush, barrier, torch, dist):
+    """Global batch 1024 split over the ranks (I = H = 256, T = 512)."""
+    from rnn_kernel_b200 import GRU, DataParallelTrainer, GraphedTrainStep
+
+    Bg, T, I, H = STRONG_GLOBAL_BATCH, 512, 256, 256
+    b = Bg // world
+    torch.manual_seed(0)
+    model = GRU(I, H).to(dev)
+    trainer = DataParallelTrainer(model, lr=1e-2)
+    g = torch.Generator(device=dev).manual_seed(2000 + rank)
+    x = torch.randn(b, T, I, device=dev, generator=g)
+    y = torch.randn(b, T, H, device=dev, generator=g)
+    for _ in range(W):
+        trainer.step(x, y)
+    graph = None
+    if not args.no_graph:
+        graph = GraphedTrainStep(trainer, [(x, y)], warmup=1,
+                                 capture_error_mode="thread_local" if world > 1 else "global")
+    barrier()
+    torch.cuda.synchronize()
+    times = timed_steps((lambda k: graph.step(0)) if graph else (lambda k: trainer.step(x, y)), K, flush, torch)
+    barrier()
+    st = step_stats(times, world, dev, torch, dist)
+    out = {"global_batch": Bg, "batch_per_gpu": b, "seq_len": T, "input_size": I, "hidden_size": H,
+           "scaling": "strong", "value": Bg * T / (st["mean"] / 1e3), "unit": UNIT,
+           "ms_per_step": st["mean"], "p50_ms": st["p50"], "p90_ms": st["p90"], "max_ms": st["max"],
+           "graph": graph is not None}
+    del graph, trainer, model, x, y
+    torch.cuda.empty_cache()
+    return out
+
+
+def dp_equivalence(world, rank, dev, barrier, torch, dist, steps=10):
+    """10 data-parallel steps (global batch 1024 split over the ranks, rank r's
+    shard from seed + r) against one GPU running the concatenated batch from
+    the same initial weights."""
+    from rnn_kernel_b200 import GRU, DataParallelTrainer
+
+    Bg, T, I, H, lr, seed = STRONG_GLOBAL_BATCH, 512, 256, 256, 1e-2, 3000
+    b = Bg // world
+    solo = dist.new_group([0])  # collective: every rank creates it
+
+    def shard(r, step):
+        g = torch.Generator(device=dev).manual_seed(seed + r + 1000 * step)
+        return (torch.randn(b, T, I, device=dev, generator=g), torch.randn(b, T, H, device=dev, generator=g))
+
+    torch.manual_seed(0)
+    model = GRU(I, H).to(dev)
+    tr = DataParallelTrainer(model, lr=lr)
+    init = tr.flat.detach().clone()
+    losses = []
+    for step in range(steps):
+        x, y = shard(rank, step)
+        loss = tr.step(x, y)
+        dist.all_reduce(loss)
+        losses.append(float(loss) / world)
+    barrier()
+    res = None
+    if rank == 0:
+        m1 = GRU(I, H).to(dev)
+        t1 = DataParallelTrainer(m1, lr=lr, process_group=solo)
+        with torch.no_grad():
+            t1.flat.copy_(init)
+        l1 = []
+        for step in range(steps):
+            xs, ys = zip(*[shard(r, step) for r in range(world)])
+            l1.append(float(t1.step(torch.cat(xs), torch.cat(ys))))
+        a, r_ = tr.flat.double(), t1.flat.double()
+        diff = (a - r_).abs()
+        lim = 1e-5 + 1e-4 * r_.abs()
+        loss_rel = max(abs(p - q) / abs(q) for p, q in zip(losses, l1))
+        res = {"steps": steps, "global_batch": Bg, "max_abs_weight_diff": float(diff.max()),
+               "worst_ratio_to_tol": float((diff / lim).max()), "loss_rel_diff": loss_rel,
+               "final_loss": l1[-1], "tolerance": "weights rtol 1e-4 / atol 1e-5 element-wise; loss rel 1e-4",
+               "pass": bool((diff <= lim).all()) and loss_rel <= 1e-4}
+        del t1, m1
+    barrier()
+    del tr, model
+    torch.cuda.empty_cache()
+    return res
+
+
+def cudnn_sweep(W, K, flush, torch):
+    """This library vs cuDNN torch.nn.GRU (TF32 off) on the same GPU, same
+    step (forward + loss + backward + SGD), median ms of K steps each."""
+    from torch import nn
+
+    from rnn_kernel_b200 import GRU
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cases = [dict(name=f"H{h}", I=h, H=h, B=64, T=256, L=1, loss="mse", h0=0.0)
+             for h in (64, 96, 128, 129, 130, 160, 192, 256)]
+    cases.append(dict(name="stacked_L2_I128_H256_B128_T1024", I=128, H=256, B=128, T=1024, L=2, loss="sumsq",
+                      h0=0.1))
+    cases.append(dict(name="B1024_I256_H256_T512", I=256, H=256, B=1024, T=512, L=1, loss="mse", h0=0.0))
+    out = []
+    for c in cases:
+        I, H, B, T, L = c["I"], c["H"], c["B"], c["T"], c["L"]
+        g = torch.Generator(device=dev).manual_seed(H)
+        x = torch.randn(B, T, I, device=dev, generator=g)
+        y = torch.randn(B, T, H, device=dev, generator=g)
+        h0 = c["h0"] * torch.randn(L, B, H, device=dev, generator=g)
+
+        def lossf(o, c=c, y=y):
+            return torch.nn.functional.mse_loss(o, y) if c["loss"] == "mse" else (o * o).sum()
+
+        torch.manual_seed(H)
+        ours = GRU(I, H, num_layers=L).to(dev)
+        ref = nn.GRU(I, H, num_layers=L, batch_first=True).to(dev)
+        with torch.no_grad():
+            for p, q in zip(ref.parameters(), ours.parameters()):
+                p.copy_(q)
+        ref.flatten_parameters()
+        res = {"case": c["name"], "I": I, "H": H, "B": B, "T": T, "layers": L}
+        for tag, m in (("ours", ours), ("cudnn", ref)):
+            opt = torch.optim.SGD(m.parameters(), lr=1e-2)
+
+            def step(k, m=m, opt=opt, x=x, h0=h0, lossf=lossf):
+                opt.zero_grad(set_to_none=True)
+                o, _ = m(x, h0)
+                lossf(o).backward()
+                opt.step()
+
+            for _ in range(W):
+                step(0)
+            torch.cuda.synchronize()
+            ts = sorted(timed_steps(step, K, flush, torch))
+            res[f"{tag}_ms"] = ts[len(ts) // 2]
+            del opt
+        res["speedup"] = res["cudnn_ms"] / res["ours_ms"]
+        out.append(res)
+        del ours, ref, x, y, h0
+        torch.cuda.empty_cache()
+    return out
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
 def main():
     args = parse()
     world, rank, local = dist_env()
@@ -263,17 +471,6 @@ def main():
         trainer.step(x, y)
     torch.cuda.synchronize()
 
-    def mean_median_max(times):
-        m = sum(times) / len(times)
-        srt = sorted(times)
-        n = len(srt)
-        md = srt[n // 2] if n % 2 else 0.5 * (srt[n // 2 - 1] + srt[n // 2])
-        if world > 1:
-            t = torch.tensor([m, md], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            m, md = float(t[0]), float(t[1])
-        return m, md
-
     # ---- eager pass: per-kernel device times (library telemetry) ----
     barrier()
     torch.cuda.synchronize()
@@ -286,14 +483,14 @@ def main():
     ktimes = _lib.timing_collect()
     torch.cuda.synchronize()
     barrier()
-    eager_ms, eager_med = mean_median_max(etimes)
+    est = step_stats(etimes, world, dev, torch, dist)
 
     # ---- headline: the same step replayed from a CUDA graph ----
     # (zero grads + fwd + loss + bwd captured; all-reduce and SGD eager).
     # Library kernels per replay = launches during capture.
     graph, graph_error, per_step_lib = None, None, 0
     cmode = "thread_local" if world > 1 else "global"
-    if not args.no_graph and not (world > 1 and not GRAPH_MULTI_GPU):
+    if not args.no_graph:
         try:
             n0 = _lib.launch_count()
             graph = GraphedTrainStep(trainer, [(x, y)], warmup=3, capture_error_mode=cmode)
@@ -301,6 +498,7 @@ def main():
         except Exception as exc:  # capture unavailable: eager headline
             graph = None
             graph_error = f"{type(exc).__name__}: {exc}"[:200]
+    graphed = graph is not None
     barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
@@ -311,7 +509,8 @@ def main():
     torch.cuda.synchronize()
     barrier()
     clocks = clk.summary()
-    ms, med = mean_median_max(times)
+    st = step_stats(times, world, dev, torch, dist)
+    ms = st["mean"]
     launches = per_step_lib * K if graph is not None else launches_eager
     value = B * world * T / (ms / 1e3)
 
@@ -366,26 +565,32 @@ def main():
                 fn(0)
             torch.cuda.synchronize()
             barrier()
-            et = timed_steps(fn, K, flush, torch)
-            ems = sum(et) / K
-            if world > 1:
-                t = torch.tensor([ems], device=dev)
-                dist.all_reduce(t, op=dist.ReduceOp.MAX)
-                ems = float(t)
-            return ems
+            return step_stats(timed_steps(fn, K, flush, torch), world, dev, torch, dist)
 
-        serial_ms = timed_e2e(e2e_serial_step)
-        ems = timed_e2e(e2e_step)
+        serial = timed_e2e(e2e_serial_step)
+        est2 = timed_e2e(e2e_step)
         while pf._queue:  # drain the outstanding prefetch
             pf.get()
         torch.cuda.synchronize()
+        ems = est2["mean"]
         e2e = {"value": B * world * T / (ems / 1e3), "unit": UNIT, "ms_per_step": ems,
+               "p50_ms": est2["p50"], "p90_ms": est2["p90"], "max_ms": est2["max"],
                "h2d_bytes_per_step": (x.numel() + y.numel()) * 4, "d2h_bytes_per_step": 4,
-               "serial_ms_per_step": serial_ms,
-               "serial_value": B * world * T / (serial_ms / 1e3),
+               "serial_ms_per_step": serial["mean"],
+               "serial_value": B * world * T / (serial["mean"] / 1e3),
                "note": "per rank: x and target copied from pinned host memory and the loss copied back every step; "
                        "next step's copy overlapped with this step on a copy stream (HostBatchPrefetcher); "
                        "serial_*: each copy issued before its own step"}
+        del pgraph, pf
+
+    del graph
+    torch.cuda.synchronize()
+
+    # ---- strong scaling (global batch 1024) and the DP equivalence check ----
+    strong = None if args.no_strong else strong_scaling(args, world, rank, dev, K, W, flush, barrier, torch, dist)
+    dp_check = None
+    if world > 1 and not args.no_dp_check:
+        dp_check = dp_equivalence(world, rank, dev, barrier, torch, dist)
 
     if rank != 0:
         if world > 1:
@@ -393,7 +598,6 @@ def main():
         return 0
 
     # ---- kernel roofline (dominant kernel, measured live in the timed region) ----
-    sm_mhz = clocks.get("sm_mhz") or 1965.0
     per_kind = {k: {"ms_per_launch": (tot / n if n else None), "launches": n, "ms_per_step": tot / K}
                 for k, (tot, n) in ktimes.items()}
     dom = max(("fwd_recurrent", "bwd_recurrent"), key=lambda k: ktimes[k][0])
@@ -401,13 +605,15 @@ def main():
     flops = recurrent_flops(B, T, H, dom == "bwd_recurrent")
     achieved = flops / (dom_ms / 1e3) / 1e12 if dom_ms else None
     peak = fp32_peak_tflops(1965.0)
-    traffic = load_traffic().get(dom)
     roofline = {
         "bound": "fp32", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-        "frac": (achieved / peak) if achieved else None, "traffic": traffic,
+        "frac": (achieved / peak) if achieved else None, "traffic": load_traffic().get(dom),
+        "traffic_source": "profiles/ncu_traffic.json: dram__bytes_read.sum + dram__bytes_write.sum of one "
+                          "full-size launch from an ncu capture of the committed kernels (not measured in this run)",
         "peak_source": "nominal FP32 CUDA-core peak 148 SM x 128 FMA/clk x 2 x 1965 MHz "
                        "(MEASURED_PEAKS.json has HBM and bf16 tensor figures only)",
         "flops_per_launch": flops,
+        "us_per_timestep": dom_ms * 1e3 / T if dom_ms else None,
     }
     t_roof = step_roofline_ms(B, T, H, 1965.0) * L
     # Side-by-side bounds: + the step's tensor-core products at 3xTF32
@@ -431,10 +637,12 @@ def main():
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
-        "ms_per_step": ms, "median_ms_per_step": med, "higher_is_better": True,
-        "graph": graph is not None, "eager_ms_per_step": eager_ms, "eager_median_ms_per_step": eager_med, "scaling": scaling, "vs_baseline": None,
+        "ms_per_step": ms, "median_ms_per_step": st["p50"], "p90_ms_per_step": st["p90"],
+        "max_ms_per_step": st["max"], "higher_is_better": True,
+        "graph": graphed, "eager_ms_per_step": est["mean"], "eager_median_ms_per_step": est["p50"],
+        "scaling": scaling, "vs_baseline": None,
         "dtype": "fp32", "data": "synthetic: x, target ~ N(0,1) per rank (seed 1000+rank); weights U(-1/16,1/16)",
-        "config": {"workload": f"gru_train_step 1-layer I={I} H={H} T={T}, batch {B}/GPU "
+        "config": {"workload": f"gru_train_step {L}-layer I={I} H={H} T={T}, batch {B}/GPU "
                                f"(fwd + MSE + bwd + allreduce + SGD lr 1e-2)",
                    "global_batch": B * world, "seq_len": T, "input_size": I, "hidden_size": H, "layers": L,
                    "parallelism": f"dp{world}", "l2": "256 MiB flush between timed steps (outside the events)"},
@@ -444,6 +652,8 @@ def main():
         "roofline": roofline,
         "step_roofline": step_roof,
         "e2e": e2e,
+        "strong": strong,
+        "dp_check": dp_check,
         "impl": "b200",
     }
     if graph_error:
@@ -472,6 +682,8 @@ def main():
                          "what": "torch.nn.GRU (cuDNN, TF32 off) same step on the same GPU",
                          "speedup_of_b200": cms / ms}
         del opt, ref
+        if not args.no_sweep:
+            line["cudnn_sweep"] = cudnn_sweep(3, 7, flush, torch)
 
     if world == 1 and not args.no_cpu_baseline:
         from oracle.cpu_baseline import time_cpu_train_step
