@@ -10,16 +10,18 @@ namespace {
 
 // Bias gradients.  dG_ih = [dr, dz, dn_pre] and dG_hh = [dr, dz, dhn] share
 // their r and z columns, so one pass sums the 3H columns of dG_ih and the n
-// block of dG_hh (virtual columns 3H .. 4H): db_ih = cols [0, 3H),
-// db_hh = [cols 0 .. 2H, cols 3H .. 4H).
-__global__ void bias_grad_partial_kernel(const float* __restrict__ dgi, const float* __restrict__ dgi_lo,
-                                         const float* __restrict__ dgh, const float* __restrict__ dgh_lo, long rows,
-                                         int H, long ld, long rchunk, double* __restrict__ part) {
+// block of dG_hh (its own buffer; virtual columns 3H .. 4H): db_ih = cols
+// [0, 3H), db_hh = [cols 0 .. 2H, cols 3H .. 4H).
+__global__ void bias_grad_partial_kernel(const float* __restrict__ dgi, const float* __restrict__ dgi_lo, long ld,
+                                         const float* __restrict__ dgn, const float* __restrict__ dgn_lo, long ldn,
+                                         long rows, int H, long rchunk, double* __restrict__ part) {
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
   if (col >= 4 * H) return;
-  // dG_hh n block = its columns 2H .. 3H; values are hi + lo
-  const float* X = col < 3 * H ? dgi + col : dgh + (col - H);
-  const float* Y = col < 3 * H ? dgi_lo + col : dgh_lo + (col - H);
+  // values are hi + lo
+  const bool ih = col < 3 * H;
+  const float* X = ih ? dgi + col : dgn + (col - 3 * H);
+  const float* Y = ih ? dgi_lo + col : dgn_lo + (col - 3 * H);
+  if (!ih) ld = ldn;
   const long r0 = blockIdx.y * rchunk, r1 = min(rows, r0 + rchunk);
   // four rows per iteration: eight independent loads in flight per thread
   double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
@@ -83,15 +85,15 @@ int transpose(const float* src, int rows, int cols, float* dst, int ldd, cudaStr
 
 size_t bias_grad_ws_bytes(int H) { return sizeof(double) * (size_t)kColChunks * 4 * H; }
 
-int bias_grads(const float* dgi, const float* dgi_lo, const float* dgh, const float* dgh_lo, long rows, int H,
-               long ld, float* db_ih, float* db_hh, void* ws, cudaStream_t stream) {
+int bias_grads(const float* dgi, const float* dgi_lo, long ld, const float* dgn, const float* dgn_lo, long ldn,
+               long rows, int H, float* db_ih, float* db_hh, void* ws, cudaStream_t stream) {
   if (H <= 0) return GRU_OK;
   const long rchunk = (rows + kColChunks - 1) / kColChunks;
   double* part = static_cast<double*>(ws);
   dim3 grid(ceil_div(4 * H, 128), kColChunks);
   LaunchScope scope(kKindColsum, stream, 2);
-  bias_grad_partial_kernel<<<grid, 128, 0, stream>>>(dgi, dgi_lo, dgh, dgh_lo, rows, H, ld, rchunk > 0 ? rchunk : 1,
-                                                   part);
+  bias_grad_partial_kernel<<<grid, 128, 0, stream>>>(dgi, dgi_lo, ld, dgn, dgn_lo, ldn, rows, H,
+                                                     rchunk > 0 ? rchunk : 1, part);
   GRU_CUDA_TRY(cudaGetLastError());
   bias_grad_final_kernel<<<ceil_div(4 * H, 8), 256, 0, stream>>>(part, kColChunks, H, db_ih, db_hh);
   GRU_CUDA_TRY(cudaGetLastError());

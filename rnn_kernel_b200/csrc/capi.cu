@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <map>
 #include <mutex>
 #include <string>
@@ -98,8 +99,8 @@ FwdLayout fwd_layout(int B, int T, int I, int H) {
 
 struct BwdLayout {
   size_t dgih, dgil, dghh, dghl, wt, wth, wtl, hph, hpl, xh, xl, gemm, col, total;
-  int ldgi;  // row stride of dG_ih / dG_hh / W_ih^T (3H rounded up to 4)
-  int ldh;   // row stride of the split h_prev copy (H rounded up to 4)
+  int ldgi;  // row stride of dG_ih / W_ih^T (3H rounded up to 4)
+  int ldh;   // row stride of the split h_prev copy and of dG_hh's n block (H rounded up to 4)
   int ldx;   // row stride of the split x copy (I rounded up to 4)
 };
 
@@ -116,8 +117,9 @@ BwdLayout bwd_layout(int B, int T, int I, int H, int device) {
   };
   take(l.dgih, (size_t)BT * l.ldgi);
   take(l.dgil, (size_t)BT * l.ldgi);
-  take(l.dghh, (size_t)BT * l.ldgi);
-  take(l.dghl, (size_t)BT * l.ldgi);
+  // only dG_hh's n block: its r and z columns are dG_ih's
+  take(l.dghh, (size_t)BT * l.ldh);
+  take(l.dghl, (size_t)BT * l.ldh);
   take(l.wt, (size_t)I * l.ldgi);
   take(l.wth, (size_t)I * l.ldgi);
   take(l.wtl, (size_t)I * l.ldgi);
@@ -126,10 +128,14 @@ BwdLayout bwd_layout(int B, int T, int I, int H, int device) {
   take(l.xh, (size_t)BT * l.ldx);
   take(l.xl, (size_t)BT * l.ldx);
   // Split-K partials of the weight-gradient products.
-  TcGemmArgs hh{nullptr, l.ldgi, nullptr, l.ldh, nullptr, H, nullptr, 3 * H, H, (int)BT, true, true};
+  // (the three products gru_backward runs: dW_hh r/z rows, dW_hh n rows, dW_ih)
+  TcGemmArgs hrz{nullptr, l.ldgi, nullptr, l.ldh, nullptr, H, nullptr, 2 * H, H, (int)BT, true, true};
+  TcGemmArgs hn{nullptr, l.ldh, nullptr, l.ldh, nullptr, H, nullptr, H, H, (int)BT, true, true};
   TcGemmArgs ih{nullptr, l.ldgi, nullptr, l.ldx, nullptr, I, nullptr, 3 * H, I, (int)BT, true, true};
   l.gemm = off;
-  off = align_up(off + std::max(tc_gemm_ws_bytes(hh, device), tc_gemm_ws_bytes(ih, device)), kAlign);
+  off = align_up(off + std::max({tc_gemm_ws_bytes(hrz, device), tc_gemm_ws_bytes(hn, device),
+                                 tc_gemm_ws_bytes(ih, device)}),
+                 kAlign);
   l.col = off;
   off = align_up(off + bias_grad_ws_bytes(H), kAlign);
   l.total = off;
@@ -290,19 +296,23 @@ int gru_backward(const float* dout, const float* dhn, const float* x, const floa
   const size_t gws_bytes = l.col - l.gemm;
   RecGeom g{};
   if ((rc = geometry(1, B, T, H, dev, &g))) return rc;
-  if ((rc = launch_rec_backward(dout, dhn, w_hh, stash, F(l.dgih), F(l.dgil), l.ldgi, F(l.dghh), F(l.dghl), dh0,
-                                g, stream)))
+  if ((rc = launch_rec_backward(dout, dhn, w_hh, stash, F(l.dgih), F(l.dgil), l.ldgi, F(l.dghh), F(l.dghl), l.ldh,
+                                dh0, g, stream)))
     return rc;
 
   const int BT = B * T;
   const int H3 = 3 * H;
   // dW_hh = dG_hh^T . h_prev (h_prev = stash column block 4), dW_ih = dG_ih^T . x
-  // on the tensor cores from pre-split copies.
+  // on the tensor cores from pre-split copies.  dW_hh's r/z rows come from
+  // dG_ih's r/z columns, its n rows from the separate n block.
   if ((rc = split_tf32(stash + 4 * H, BT, H, 5L * H, F(l.hph), F(l.hpl), l.ldh, stream))) return rc;
   if ((rc = split_tf32(x, BT, I, I, F(l.xh), F(l.xl), l.ldx, stream))) return rc;
-  TcGemmArgs hh{F(l.dghh), l.ldgi, F(l.hph), l.ldh, dw_hh, H, nullptr, H3, H, BT, true, true, F(l.dghl), F(l.hpl)};
+  TcGemmArgs hrz{F(l.dgih), l.ldgi, F(l.hph), l.ldh, dw_hh, H, nullptr, 2 * H, H, BT, true, true, F(l.dgil), F(l.hpl)};
+  TcGemmArgs hn{F(l.dghh), l.ldh, F(l.hph), l.ldh, dw_hh + 2L * H * H, H, nullptr, H, H, BT, true, true, F(l.dghl),
+                F(l.hpl)};
   TcGemmArgs ih{F(l.dgih), l.ldgi, F(l.xh), l.ldx, dw_ih, I, nullptr, H3, I, BT, true, true, F(l.dgil), F(l.xl)};
-  if ((rc = tc_gemm(hh, stream, kKindGradGemm, gws, gws_bytes))) return rc;
+  if ((rc = tc_gemm(hrz, stream, kKindGradGemm, gws, gws_bytes))) return rc;
+  if ((rc = tc_gemm(hn, stream, kKindGradGemm, gws, gws_bytes))) return rc;
   if ((rc = tc_gemm(ih, stream, kKindGradGemm, gws, gws_bytes))) return rc;
   if (dx) {
     // dx = dG_ih . W_ih, with W_ih^T staged (and split) as [I, ldgi].
@@ -311,8 +321,8 @@ int gru_backward(const float* dout, const float* dhn, const float* x, const floa
     TcGemmArgs a3{F(l.dgih), l.ldgi, F(l.wth), l.ldgi, dx, I, nullptr, BT, I, H3, false, false, F(l.dgil), F(l.wtl)};
     if ((rc = tc_gemm(a3, stream, kKindGradGemm))) return rc;
   }
-  if ((rc = bias_grads(F(l.dgih), F(l.dgil), F(l.dghh), F(l.dghl), BT, H, l.ldgi, db_ih, db_hh, ws + l.col,
-                       stream)))
+  if ((rc = bias_grads(F(l.dgih), F(l.dgil), l.ldgi, F(l.dghh), F(l.dghl), l.ldh, BT, H, db_ih, db_hh,
+                       ws + l.col, stream)))
     return rc;
   return GRU_OK;
 }

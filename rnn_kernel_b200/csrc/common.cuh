@@ -62,10 +62,11 @@ int rec_backward_geometry(int B, int T, int H, int device, RecGeom* g);
 int launch_rec_forward(const float* G, int ldg, const float* h0, const float* w_hh, const float* b_hh,
                        float* out, float* hn, float* stash, const RecGeom& g,
                        cudaStream_t stream);
-// dG_ih / dG_hh are written pre-split (hi, lo) with row stride ldgi.
+// dG_ih [rows, 3H] (row stride ldgi) and the n block of dG_hh [rows, H] (row
+// stride ldgn) are written pre-split (hi, lo).
 int launch_rec_backward(const float* dout, const float* dhn, const float* w_hh,
                         const float* stash, float* dGi, float* dGi_lo, int ldgi, float* dGh, float* dGh_lo,
-                        float* dh0,
+                        int ldgn, float* dh0,
                         const RecGeom& g, cudaStream_t stream);
 
 // Tensor-core (tcgen05, 3xTF32) product C[m, n] = sum_k A(m, k) B(n, k) (+ bias).
@@ -99,12 +100,13 @@ int read_gemm_status(int reset, int* status);
 int transpose(const float* src, int rows, int cols, float* dst, int ldd, cudaStream_t stream);
 
 // Bias gradients db_ih = colsum(dG_ih), db_hh = colsum(dG_hh) over `rows`
-// rows of row stride ld (FP64 accumulation, deterministic two-pass; the
-// shared r/z columns are summed once).  ws needs bias_grad_ws_bytes(H).
+// rows (FP64 accumulation, deterministic two-pass).  dG_hh's r/z columns are
+// dG_ih's, so only its n block dgn [rows, H] (row stride ldn) is passed.
+// ws needs bias_grad_ws_bytes(H).
 size_t bias_grad_ws_bytes(int H);
 // dG given pre-split: the values summed are hi + lo.
-int bias_grads(const float* dgi, const float* dgi_lo, const float* dgh, const float* dgh_lo, long rows, int H,
-               long ld, float* db_ih, float* db_hh, void* ws, cudaStream_t stream);
+int bias_grads(const float* dgi, const float* dgi_lo, long ld, const float* dgn, const float* dgn_lo, long ldn,
+               long rows, int H, float* db_ih, float* db_hh, void* ws, cudaStream_t stream);
 
 int sm_count(int device);
 

@@ -148,8 +148,9 @@ struct Smem {
   static constexpr int kBTile = BN * kBK * 4;
   static constexpr int kStage = 2 * kATile + 2 * kBTile;  // A hi, A lo, B hi, B lo
   static constexpr int kBarOff = S * kStage;
-  // per drain warp a 32 x 16 epilogue staging block (row pitch 17 floats)
-  static constexpr int kEpiPitch = 17;
+  // per drain warp a 32 x 16 epilogue staging block (row pitch 16 floats,
+  // 16-byte chunks XOR-swizzled by row, see the epilogue)
+  static constexpr int kEpiPitch = 16;
   static constexpr int kEpiOff = kBarOff + 256;
   static constexpr int kBytes = kEpiOff + kDrainWarps * 32 * kEpiPitch * 4 + 1024;  // + alignment slack
 };
@@ -371,21 +372,34 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ah, const __grid_cons
         // Each lane holds one row; stage 16 columns at a time through this
         // warp's shared block and store them with 4 lanes per row (64
         // contiguous bytes, 8 rows per instruction) instead of one 16-byte
-        // piece of 32 different rows per instruction.
+        // piece of 32 different rows per instruction.  Row r keeps its four
+        // 16-byte chunks q at chunk slot q ^ ((r >> 1) & 3): the lane-per-row
+        // float4 writes and the 4-lanes-per-row float4 reads then both touch
+        // 8 distinct 16-byte bank groups per quarter warp (no conflicts).
         float* eb = reinterpret_cast<float*>(smem + L::kEpiOff) + (warp - 2) * (32 * L::kEpiPitch);
         const int rbase = w.m0 + 32 * quarter;
+        const int wsw = (lane >> 1) & 3;
 #pragma unroll
         for (int c0 = 0; c0 < kCW; c0 += 16) {
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) eb[lane * L::kEpiPitch + jj] = acc[c0 + jj] + (bu ? bu[n0 + c0 + jj] : 0.0f);
+          for (int q = 0; q < 4; ++q) {
+            const int c = c0 + 4 * q;
+            float4 v = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
+            if (bu) {
+              v.x += bu[n0 + c];
+              v.y += bu[n0 + c + 1];
+              v.z += bu[n0 + c + 2];
+              v.w += bu[n0 + c + 3];
+            }
+            *reinterpret_cast<float4*>(eb + lane * L::kEpiPitch + 4 * (q ^ wsw)) = v;
+          }
           __syncwarp();
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const int r = i * 8 + (lane >> 2), cc = (lane & 3) * 4;
+            const int r = i * 8 + (lane >> 2), q = lane & 3;
             if (rbase + r < M) {
-              const float* e = eb + r * L::kEpiPitch + cc;
-              *reinterpret_cast<float4*>(Cu + (long)(rbase + r) * ldc + n0 + c0 + cc) =
-                  make_float4(e[0], e[1], e[2], e[3]);
+              const float4 e = *reinterpret_cast<const float4*>(eb + r * L::kEpiPitch + 4 * (q ^ ((r >> 1) & 3)));
+              *reinterpret_cast<float4*>(Cu + (long)(rbase + r) * ldc + n0 + c0 + 4 * q) = e;
             }
           }
           __syncwarp();

@@ -428,13 +428,16 @@ struct BwdArgs {
   const float* dhn;    // [B,H] or null
   const float* w_hh;   // [3H,H]
   const float* stash;  // [B,T,5H]
-  // dG_ih / dG_hh [B,T,3H] (row stride ldgi), each written pre-split for the
-  // tensor-core products: hi = tf32(v), lo = tf32(v - hi).
+  // dG_ih [B,T,3H] (row stride ldgi) and the n block of dG_hh [B,T,H] (row
+  // stride ldgn; its r and z blocks equal dG_ih's and are not stored), each
+  // written pre-split for the tensor-core products: hi = tf32(v),
+  // lo = tf32(v - hi).
   float* dGi;
   float* dGi_lo;
   int ldgi;
   float* dGh;
   float* dGh_lo;
+  int ldgn;
   float* dh0;          // [B,H]
 };
 
@@ -650,13 +653,11 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
         dgs[(s * 3 + 2) * 32 + jl] = dhn_gate;
         gz[b * Hc + jl] = gg * z;
         const size_t row = (size_t)(b_begin + b) * T + t;
-        const size_t o = row * a.ldgi + j;
+        const size_t o = row * a.ldgi + j, on = row * a.ldgn + j;
         split_store(a.dGi + o, a.dGi_lo + o, dr_pre);
         split_store(a.dGi + o + H, a.dGi_lo + o + H, dz_pre);
         split_store(a.dGi + o + 2 * H, a.dGi_lo + o + 2 * H, dn_pre);
-        split_store(a.dGh + o, a.dGh_lo + o, dr_pre);
-        split_store(a.dGh + o + H, a.dGh_lo + o + H, dz_pre);
-        split_store(a.dGh + o + 2 * H, a.dGh_lo + o + 2 * H, dhn_gate);
+        split_store(a.dGh + on, a.dGh_lo + on, dhn_gate);
       }
       __syncthreads();
       // Every thread has consumed slot `rslot`: re-arm it for iteration it+2
@@ -926,8 +927,8 @@ int launch_rec_forward(const float* G, int ldg, const float* h0, const float* w_
 
 int launch_rec_backward(const float* dout, const float* dhn, const float* w_hh,
                         const float* stash, float* dGi, float* dGi_lo, int ldgi, float* dGh, float* dGh_lo,
-                        float* dh0, const RecGeom& g, cudaStream_t stream) {
-  BwdArgs a{dout, dhn, w_hh, stash, dGi, dGi_lo, ldgi, dGh, dGh_lo, dh0};
+                        int ldgn, float* dh0, const RecGeom& g, cudaStream_t stream) {
+  BwdArgs a{dout, dhn, w_hh, stash, dGi, dGi_lo, ldgi, dGh, dGh_lo, ldgn, dh0};
   RecGeom gg = g;
   if ((reinterpret_cast<uintptr_t>(dout) | reinterpret_cast<uintptr_t>(stash)) & 15) gg.vec4 = 0;
   return launch_clusters(kernel_for(false, gg.R), a, gg, stream, kKindBwdRecurrent);
