@@ -286,8 +286,10 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
     for (int k = 0; k < kPlanItems; ++k) plan_dst[k] = plan_off[k] = 0;
     if (pstride > 0 && nb * 3 * hw > kPlanItems * pstride) cpe = 3;
     const int n = nb * (3 / cpe) * hw;
-    // more than kPlanItems entries, or offsets beyond 32 bits: no plan
-    if ((pfirst >= 0 && pfirst + kPlanItems * pstride < n) || (size_t)nb * T * ldg >= (1ull << 31)) plan_n = -1;
+    // more than kPlanItems entries per issuing thread, or offsets beyond 32
+    // bits: no plan.  The decision must be the same for every thread of the
+    // CTA (a planned and an unplanned thread index the items differently).
+    if (kPlanItems * pstride < n || (size_t)nb * T * ldg >= (1ull << 31)) plan_n = -1;
     if (pfirst >= 0 && plan_n == 0) {
 #pragma unroll
       for (int k = 0; k < kPlanItems; ++k) {
@@ -549,9 +551,8 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
     for (int k = 0; k < kPlanItems; ++k) plan_dst[k] = plan_offd[k] = plan_offs[k] = plan_q0[k] = 0;
     while (cpe < 6 && nb * (6 / cpe) * hw > kPlanItems * pstride) cpe = cpe == 1 ? 2 : (cpe == 2 ? 3 : 6);
     const int per = 6 / cpe, n = nb * per * hw;
-    if (a.dout == nullptr || (pfirst >= 0 && pfirst + kPlanItems * pstride < n) ||
-        (size_t)nb * T * 5 * H >= (1ull << 31))
-      plan_n = -1;
+    // same rule as the forward: a CTA-uniform decision
+    if (a.dout == nullptr || kPlanItems * pstride < n || (size_t)nb * T * 5 * H >= (1ull << 31)) plan_n = -1;
     if (pfirst >= 0 && plan_n == 0) {
 #pragma unroll
       for (int k = 0; k < kPlanItems; ++k) {

@@ -92,6 +92,15 @@ def test_large_batch_h256_two_waves():
     assert_parity(mine, theirs, truth, weights="envelope")
 
 
+@pytest.mark.parametrize("B,T,H", [(330, 12, 256), (512, 10, 256), (400, 9, 256), (1024, 9, 256), (3000, 10, 64)])
+def test_large_batch_time_loop_prefetch(B, T, H):
+    # Sequences longer than the prologue of the per-step input prefetch (the
+    # time loops' own prefetch then runs) with many rows per cluster, some of
+    # whose last sub-chunks leave few idle threads to issue it.
+    mine, theirs, truth = run_pair(16, H, 1, B, T, seed=B + T)
+    assert_parity(mine, theirs, truth, weights="envelope")
+
+
 def test_hn_only_loss_grad_output_none():
     mine, theirs, truth = run_pair(6, 48, 2, 3, 7, seed=5, loss="hn_only")
     assert_parity(mine, theirs, truth)
