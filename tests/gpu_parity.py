@@ -17,15 +17,16 @@ terms of size ~1, and the FP32 rounding of the forward activations alone moves
 some entries by more than 1e-5 + 1e-4*|value| from the FP64 truth: torch FP32
 itself misses that element-wise bar by up to 8x at I=H=256, B=64, T=512.  For
 those tensors ``weights="envelope"`` requires the max error against the truth
-to stay within 3x of torch FP32's own (plus atol) and the normwise relative
-error ||ours - truth||_F / ||truth||_F to stay below 1e-6.  The factor
-is not 1 because
-the input projection and dx run on the tensor cores, whose FP32 accumulation
-truncates.  The GEMM drains a fresh accumulator per 32-wide K stage into FP32
-registers, which leaves a measured relative shrink bias of -8.6e-8 on
-G = x.W_ih^T (FP32 FMA: ~0); summed coherently in dW_ih = sum dG_ih * x over
-B*T = 131k terms (2 layers, B=128, T=1024) that stays inside the envelope.
-Every other tensor stays strict.
+to stay within ``factor`` times torch FP32's own (plus atol) and the normwise
+relative error ||ours - truth||_F / ||truth||_F to stay below 1e-6; the
+per-tensor ratio is printed (pytest -s).  ``factor`` is 1 except for the
+stacked 2-layer shape (B*T = 131k), measured at 2.2x (dW_ih, layer 0) and
+1.5x (layer 1): the input projection and dx run on the tensor cores, whose
+FP32 accumulation inside one 32-wide K stage truncates (round toward zero),
+a bias that adds up coherently over the K = B*T terms of dW_ih = sum dG_ih x
+while FP32 rounding grows like sqrt(K); every other weight/bias gradient of
+every case measures <= 0.7x torch FP32's error.  Every other tensor stays
+strict.
 """
 from __future__ import annotations
 
@@ -74,23 +75,24 @@ def run_pair(I, H, L, B, T, seed, loss="random", h0_scale=1.0, ref_dtype=torch.f
     return mine, theirs, t64
 
 
-def _envelope_ok(a, t32, t64, atol):
+def _envelope_ok(a, t32, t64, atol, factor):
     e_ours = (a - t64).abs()
     e_ref = (t32 - t64).abs()
     rms = lambda e: float(e.pow(2).mean().sqrt())
     norm_rel = float((a - t64).norm() / t64.norm().clamp_min(1e-30))
-    ok = float(e_ours.max()) <= 3.0 * float(e_ref.max()) + atol and norm_rel <= 1e-6
+    ok = float(e_ours.max()) <= factor * float(e_ref.max()) + atol and norm_rel <= 1e-6
     return ok, (float(e_ours.max()), norm_rel), (float(e_ref.max()), rms(e_ref))
 
 
-def assert_parity(mine, t32, t64=None, rtol=RTOL, atol=ATOL, weights="strict"):
+def assert_parity(mine, t32, t64=None, rtol=RTOL, atol=ATOL, weights="strict", factor=1.0):
     bad = []
     for k in t32:
         if weights == "envelope" and k.startswith(("dweight", "dbias")) and t64 is not None:
-            ok, eo, er = _envelope_ok(mine[k], t32[k], t64[k], atol)
+            ok, eo, er = _envelope_ok(mine[k], t32[k], t64[k], atol, factor)
+            print(f"{k}: max error {eo[0] / max(er[0], 1e-300):.2f}x torch fp32's, normwise {eo[1]:.1e}")
             if not ok:
-                bad.append(f"{k}: error vs fp64 truth max {eo[0]:.3e} (3x torch fp32's {er[0]:.3e} allowed), "
-                           f"normwise relative {eo[1]:.2e} (1e-6 allowed)")
+                bad.append(f"{k}: error vs fp64 truth max {eo[0]:.3e} ({factor}x torch fp32's {er[0]:.3e} "
+                           f"allowed), normwise relative {eo[1]:.2e} (1e-6 allowed)")
             continue
         a, b = mine[k], t32[k]
         assert a.shape == b.shape, (k, a.shape, b.shape)

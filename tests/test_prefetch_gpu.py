@@ -68,7 +68,8 @@ def test_training_through_prefetcher_matches_device_inputs():
     assert torch.equal(w1, w2)
 
 
-def test_graphed_steps_match_eager_steps():
+@pytest.mark.parametrize("layers", [1, 2])
+def test_graphed_steps_match_eager_steps(layers):
     from rnn_kernel_b200 import GraphedTrainStep
 
     dev = torch.device("cuda", 0)
@@ -77,7 +78,7 @@ def test_graphed_steps_match_eager_steps():
 
     def make():
         torch.manual_seed(21)
-        return DataParallelTrainer(GRU(24, 40, num_layers=2).to(dev), lr=1e-2)
+        return DataParallelTrainer(GRU(24, 40, num_layers=layers).to(dev), lr=1e-2)
 
     # eager reference: 3 warm-up steps on batch 0 (what the capture warm-up
     # does), then one step per batch
