@@ -104,7 +104,7 @@ struct BwdLayout {
   int ldx;   // row stride of the split x copy (I rounded up to 4)
 };
 
-BwdLayout bwd_layout(int B, int T, int I, int H, int device) {
+BwdLayout bwd_layout(int B, int T, int I, int H, int device, int nclusters) {
   const long BT = (long)B * T;
   BwdLayout l{};
   l.ldgi = pad4(3 * H);
@@ -136,8 +136,9 @@ BwdLayout bwd_layout(int B, int T, int I, int H, int device) {
   off = align_up(off + std::max({tc_gemm_ws_bytes(hrz, device), tc_gemm_ws_bytes(hn, device),
                                  tc_gemm_ws_bytes(ih, device)}),
                  kAlign);
+  // per-cluster FP64 bias-gradient partials written by the backward time loop
   l.col = off;
-  off = align_up(off + bias_grad_ws_bytes(H), kAlign);
+  off = align_up(off + sizeof(double) * (size_t)nclusters * 4 * H, kAlign);
   l.total = off;
   return l;
 }
@@ -213,7 +214,9 @@ size_t gru_backward_workspace_bytes(int B, int T, int I, int H) {
     cudaGetLastError();
     dev = 0;
   }
-  return bwd_layout(B, T, I, H, dev).total;
+  RecGeom g{};
+  if (geometry(1, B, T, H, dev, &g) != GRU_OK) return 0;
+  return bwd_layout(B, T, I, H, dev, g.nclusters).total;
 }
 
 int gru_forward(const float* x, const float* h0, const float* w_ih, const float* w_hh,
@@ -285,7 +288,9 @@ int gru_backward(const float* dout, const float* dhn, const float* x, const floa
     set_error("gru_backward: null input pointer");
     return GRU_ERR_INVALID;
   }
-  const BwdLayout l = bwd_layout(B, T, I, H, dev);
+  RecGeom g{};
+  if ((rc = geometry(1, B, T, H, dev, &g))) return rc;
+  const BwdLayout l = bwd_layout(B, T, I, H, dev, g.nclusters);
   if (!workspace || workspace_bytes < l.total) {
     set_error("gru_backward: workspace too small");
     return GRU_ERR_INVALID;
@@ -294,10 +299,9 @@ int gru_backward(const float* dout, const float* dhn, const float* x, const floa
   auto F = [&](size_t off) { return reinterpret_cast<float*>(ws + off); };
   void* gws = ws + l.gemm;
   const size_t gws_bytes = l.col - l.gemm;
-  RecGeom g{};
-  if ((rc = geometry(1, B, T, H, dev, &g))) return rc;
+  double* dbpart = reinterpret_cast<double*>(ws + l.col);
   if ((rc = launch_rec_backward(dout, dhn, w_hh, stash, F(l.dgih), F(l.dgil), l.ldgi, F(l.dghh), F(l.dghl), l.ldh,
-                                dh0, g, stream)))
+                                dh0, dbpart, g, stream)))
     return rc;
 
   const int BT = B * T;
@@ -321,9 +325,7 @@ int gru_backward(const float* dout, const float* dhn, const float* x, const floa
     TcGemmArgs a3{F(l.dgih), l.ldgi, F(l.wth), l.ldgi, dx, I, nullptr, BT, I, H3, false, false, F(l.dgil), F(l.wtl)};
     if ((rc = tc_gemm(a3, stream, kKindGradGemm))) return rc;
   }
-  if ((rc = bias_grads(F(l.dgih), F(l.dgil), l.ldgi, F(l.dghh), F(l.dghl), l.ldh, BT, H, db_ih, db_hh,
-                       ws + l.col, stream)))
-    return rc;
+  if ((rc = bias_grads_finish(dbpart, g.nclusters, H, db_ih, db_hh, stream))) return rc;
   return GRU_OK;
 }
 

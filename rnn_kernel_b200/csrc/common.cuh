@@ -45,7 +45,7 @@ struct RecGeom {
   int max_clusters;  // clusters of this kernel resident at once on the device
   // Shared-memory layout, offsets in floats from the dynamic base; every
   // region starts on a 16-byte boundary (float4 accesses).
-  int off1, off2, off3;
+  int off1, off2, off3, off4;
   int vec4;  // per-step input rows are 16-byte aligned (H, Hc multiples of 4)
   size_t smem;  // dynamic shared memory bytes per CTA
 };
@@ -66,7 +66,7 @@ int launch_rec_forward(const float* G, int ldg, const float* h0, const float* w_
 // stride ldgn) are written pre-split (hi, lo).
 int launch_rec_backward(const float* dout, const float* dhn, const float* w_hh,
                         const float* stash, float* dGi, float* dGi_lo, int ldgi, float* dGh, float* dGh_lo,
-                        int ldgn, float* dh0,
+                        int ldgn, float* dh0, double* dbpart,
                         const RecGeom& g, cudaStream_t stream);
 
 // Tensor-core (tcgen05, 3xTF32) product C[m, n] = sum_k A(m, k) B(n, k) (+ bias).
@@ -99,14 +99,11 @@ int read_gemm_status(int reset, int* status);
 // Transpose a [rows, cols] matrix into [cols, ldd] (columns rows .. ldd zeroed).
 int transpose(const float* src, int rows, int cols, float* dst, int ldd, cudaStream_t stream);
 
-// Bias gradients db_ih = colsum(dG_ih), db_hh = colsum(dG_hh) over `rows`
-// rows (FP64 accumulation, deterministic two-pass).  dG_hh's r/z columns are
-// dG_ih's, so only its n block dgn [rows, H] (row stride ldn) is passed.
-// ws needs bias_grad_ws_bytes(H).
-size_t bias_grad_ws_bytes(int H);
-// dG given pre-split: the values summed are hi + lo.
-int bias_grads(const float* dgi, const float* dgi_lo, long ld, const float* dgn, const float* dgn_lo, long ldn,
-               long rows, int H, float* db_ih, float* db_hh, void* ws, cudaStream_t stream);
+// Bias gradients from the backward time loop's per-cluster FP64 partials
+// part [nparts][4H] (cols [0, 3H): colsums of dG_ih; [3H, 4H): of dG_hh's n
+// block; dG_hh's r/z columns are dG_ih's): db_ih = cols [0, 3H), db_hh =
+// cols [0, 2H) and [3H, 4H); summed in a fixed order (deterministic).
+int bias_grads_finish(const double* part, int nparts, int H, float* db_ih, float* db_hh, cudaStream_t stream);
 
 int sm_count(int device);
 

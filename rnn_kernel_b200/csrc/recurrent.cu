@@ -441,6 +441,10 @@ struct BwdArgs {
   float* dGh_lo;
   int ldgn;
   float* dh0;          // [B,H]
+  // Bias-gradient partial sums of this launch, one row of 4H per cluster
+  // (cols [0, 3H): dG_ih's r, z, n columns; [3H, 4H): dG_hh's n block),
+  // accumulated on chip in FP64 over every (b, t) of the cluster.
+  double* dbpart;
 };
 
 template <int R>
@@ -491,6 +495,10 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
   for (int e = tid; e < 2 * red_slot; e += nthr) red[e] = 0.0f;
   for (int e = tid; e < bcp * Hc; e += nthr) gz[e] = 0.0f;
   for (int e = tid; e < R * 3 * 32; e += nthr) dgs[e] = 0.0f;
+  // FP64 sums of dr, dz, dn_pre, dhn per (sub-chunk row s, unit): each is
+  // owned by the one thread that computes that item in every step
+  double* dbacc = reinterpret_cast<double*>(smem + g.off4);  // [R][4][Hc]
+  for (int e = tid; e < R * 4 * Hc; e += nthr) dbacc[e] = 0.0;
   const uint32_t bar0 = smem_u32(&mbar[0]);
   const uint32_t bytes_per_step = (uint32_t)(C * nb * hcnt * 4);
   if (tid == 0) {
@@ -659,6 +667,11 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
         split_store(a.dGi + o + H, a.dGi_lo + o + H, dz_pre);
         split_store(a.dGi + o + 2 * H, a.dGi_lo + o + 2 * H, dn_pre);
         split_store(a.dGh + on, a.dGh_lo + on, dhn_gate);
+        double* acc = dbacc + (s * 4) * Hc + jl;
+        acc[0] += (double)dr_pre;
+        acc[Hc] += (double)dz_pre;
+        acc[2 * Hc] += (double)dn_pre;
+        acc[3 * Hc] += (double)dhn_gate;
       }
       __syncthreads();
       // Every thread has consumed slot `rslot`: re-arm it for iteration it+2
@@ -727,6 +740,15 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
       }
     }
   }
+  // This cluster's bias-gradient partials: the sub-chunk rows' sums added in
+  // a fixed order (deterministic), this CTA's units of the four blocks.
+  __syncthreads();
+  for (int e = tid; e < 4 * hcnt; e += nthr) {
+    const int q = e / hcnt, jl = e - q * hcnt;
+    double sum = 0.0;
+    for (int s = 0; s < R; ++s) sum += dbacc[(s * 4 + q) * Hc + jl];
+    a.dbpart[(size_t)cid * 4 * H + q * H + j0 + jl] = sum;
+  }
   cp_async_wait<0>();
   cluster.sync();
 }
@@ -756,7 +778,8 @@ size_t bwd_smem(RecGeom& g) {
   g.off1 = round4((size_t)2 * g.C * g.bcp * g.Hc);
   g.off2 = g.off1 + round4((size_t)g.bcp * g.Hc);
   g.off3 = g.off2 + round4((size_t)g.R * 3 * 32);
-  return sizeof(float) * (size_t)(g.off3 + round4((size_t)g.pd * g.bcp * 6 * g.Hc));
+  g.off4 = g.off3 + round4((size_t)g.pd * g.bcp * 6 * g.Hc);
+  return sizeof(float) * (size_t)(g.off4 + (size_t)8 * g.R * g.Hc);  // + FP64 [R][4][Hc]
 }
 
 template <int R>
@@ -841,7 +864,7 @@ int finish_geometry(RecGeom* g, int device, bool fwd, SmemFn smem_of) {
     g->nclusters = ceil_div(g->B, g->bc);
   }
   g->smem = smem_of(*g);
-  if ((g->off1 | g->off2 | g->off3) & 3) {
+  if ((g->off1 | g->off2 | g->off3 | g->off4) & 3) {
     set_error("internal: recurrent shared-memory region not 16-byte aligned");
     return GRU_ERR_INVALID;
   }
@@ -928,8 +951,8 @@ int launch_rec_forward(const float* G, int ldg, const float* h0, const float* w_
 
 int launch_rec_backward(const float* dout, const float* dhn, const float* w_hh,
                         const float* stash, float* dGi, float* dGi_lo, int ldgi, float* dGh, float* dGh_lo,
-                        int ldgn, float* dh0, const RecGeom& g, cudaStream_t stream) {
-  BwdArgs a{dout, dhn, w_hh, stash, dGi, dGi_lo, ldgi, dGh, dGh_lo, ldgn, dh0};
+                        int ldgn, float* dh0, double* dbpart, const RecGeom& g, cudaStream_t stream) {
+  BwdArgs a{dout, dhn, w_hh, stash, dGi, dGi_lo, ldgi, dGh, dGh_lo, ldgn, dh0, dbpart};
   RecGeom gg = g;
   if ((reinterpret_cast<uintptr_t>(dout) | reinterpret_cast<uintptr_t>(stash)) & 15) gg.vec4 = 0;
   return launch_clusters(kernel_for(false, gg.R), a, gg, stream, kKindBwdRecurrent);
