@@ -29,6 +29,7 @@ sides; per-step statistics are the max over ranks.
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import os
 import subprocess
@@ -85,7 +86,7 @@ class ClockSampler:
 
     NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def __init__(self, cuda_index: int, period_s: float = 0.002):
+    def __init__(self, cuda_index: int, period_s: float = 0.005):
         self.cuda_index = cuda_index
         self.period = period_s
         self.rows = []  # (sm_mhz, max_mhz, power_w, [reason flags])
@@ -307,7 +308,8 @@ def strong_scaling(args, world, rank, dev, K, W, flush, barrier, torch, dist):
     graph = None
     if not args.no_graph:
         graph = GraphedTrainStep(trainer, [(x, y)], warmup=1,
-                                 capture_error_mode="thread_local" if world > 1 else "global")
+                                 capture_error_mode="thread_local" if world > 1 else "global",
+                                 include_update=world == 1)
     barrier()
     torch.cuda.synchronize()
     times = timed_steps((lambda k: graph.step(0)) if graph else (lambda k: trainer.step(x, y)), K, flush, torch)
@@ -486,14 +488,17 @@ def main():
     est = step_stats(etimes, world, dev, torch, dist)
 
     # ---- headline: the same step replayed from a CUDA graph ----
-    # (zero grads + fwd + loss + bwd captured; all-reduce and SGD eager).
-    # Library kernels per replay = launches during capture.
+    # (zero grads + fwd + loss + bwd captured, and at N = 1 the SGD update
+    # too: one launch per step; at N > 1 the NCCL all-reduce and the update
+    # run eagerly after the replay).  Library kernels per replay = launches
+    # during capture.
     graph, graph_error, per_step_lib = None, None, 0
     cmode = "thread_local" if world > 1 else "global"
     if not args.no_graph:
         try:
             n0 = _lib.launch_count()
-            graph = GraphedTrainStep(trainer, [(x, y)], warmup=3, capture_error_mode=cmode)
+            graph = GraphedTrainStep(trainer, [(x, y)], warmup=3, capture_error_mode=cmode,
+                                     include_update=world == 1)
             per_step_lib = (_lib.launch_count() - n0) - 3 * (launches_eager // K)
         except Exception as exc:  # capture unavailable: eager headline
             graph = None
@@ -501,14 +506,16 @@ def main():
     graphed = graph is not None
     barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
+    # only rank 0 reports clocks: the other ranks do not poll NVML (8 processes
+    # polling the driver at once stalled host threads)
+    with (ClockSampler(local) if rank == 0 else contextlib.nullcontext()) as clk:
         if graph is not None:
             times = timed_steps(lambda k: graph.step(0), K, flush, torch)
         else:
             times = timed_steps(lambda k: trainer.step(x, y), K, flush, torch)
     torch.cuda.synchronize()
     barrier()
-    clocks = clk.summary()
+    clocks = clk.summary() if rank == 0 else None
     st = step_stats(times, world, dev, torch, dist)
     ms = st["mean"]
     launches = per_step_lib * K if graph is not None else launches_eager
@@ -549,7 +556,8 @@ def main():
                 pf.put(xh, yh)
                 pf.get()
             torch.cuda.synchronize()
-            pgraph = GraphedTrainStep(trainer, [pf._bufs[0], pf._bufs[1]], warmup=1, capture_error_mode=cmode)
+            pgraph = GraphedTrainStep(trainer, [pf._bufs[0], pf._bufs[1]], warmup=1, capture_error_mode=cmode,
+                                      include_update=world == 1)
             torch.cuda.synchronize()
         pf.put(xh, yh)  # one batch ahead from here on
 

@@ -156,8 +156,13 @@ class GraphedTrainStep:
 
     The device work of zeroing the gradients, the forward, the loss and the
     backward (this library's kernels and torch's) is captured once per static
-    input pair and replayed with one launch; the gradient all-reduce and the
-    SGD update run eagerly after each replay, so no collective is captured.
+    input pair and replayed with one launch.  With ``include_update`` the
+    gradient all-reduce (NCCL, captured into the graph) and the SGD update
+    are part of the same graph, so a whole train step is one launch and no
+    host work sits between its kernels; otherwise they run eagerly after each
+    replay.  ``include_update`` is meant for a single process: capturing the
+    NCCL all-reduce was measured to hang a 2-process run here, so with a
+    process group keep the all-reduce eager.
     ``inputs`` lists the static ``(x, target)`` device tensor pairs (for
     instance the two buffer sets of a :class:`HostBatchPrefetcher`);
     ``step(i)`` replays graph ``i`` on whatever those tensors hold now.
@@ -171,8 +176,9 @@ class GraphedTrainStep:
     """
 
     def __init__(self, trainer: DataParallelTrainer, inputs, warmup: int = 3,
-                 capture_error_mode: str = "global") -> None:
+                 capture_error_mode: str = "global", include_update: bool = False) -> None:
         self.trainer = trainer
+        self.include_update = include_update
         trainer.overlap_active = False
         trainer._pending = [n for _, _, n in trainer._buckets]
         trainer._works = []
@@ -190,12 +196,15 @@ class GraphedTrainStep:
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, capture_error_mode=capture_error_mode):
                 loss = trainer.forward_backward(x, y)
+                if include_update:
+                    trainer.reduce_and_update()
             self.graphs.append(g)
             self.losses.append(loss)
 
     def step(self, i: int = 0) -> torch.Tensor:
         self.graphs[i].replay()
-        self.trainer.reduce_and_update()
+        if not self.include_update:
+            self.trainer.reduce_and_update()
         return self.losses[i]
 
     def close(self) -> None:

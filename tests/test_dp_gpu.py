@@ -64,7 +64,7 @@ def _worker(rank, world, port, out_path, layers=1, graphed=False):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("layers,graphed", [(1, False), (2, False), (2, True)])
+@pytest.mark.parametrize("layers,graphed", [(1, False), (2, False), (2, "replay")])
 def test_dp_two_gpus_matches_single_gpu(layers, graphed):
     from rnn_kernel_b200 import GRU, DataParallelTrainer
 

@@ -68,8 +68,8 @@ def test_training_through_prefetcher_matches_device_inputs():
     assert torch.equal(w1, w2)
 
 
-@pytest.mark.parametrize("layers", [1, 2])
-def test_graphed_steps_match_eager_steps(layers):
+@pytest.mark.parametrize("layers,include_update", [(1, False), (2, False), (1, True), (2, True)])
+def test_graphed_steps_match_eager_steps(layers, include_update):
     from rnn_kernel_b200 import GraphedTrainStep
 
     dev = torch.device("cuda", 0)
@@ -90,7 +90,7 @@ def test_graphed_steps_match_eager_steps(layers):
 
     tr = make()
     xs, ys = x0.clone(), y0.clone()
-    gs = GraphedTrainStep(tr, [(xs, ys)], warmup=3)
+    gs = GraphedTrainStep(tr, [(xs, ys)], warmup=3, include_update=include_update)
     losses = []
     for x, y in host:
         xs.copy_(x)
