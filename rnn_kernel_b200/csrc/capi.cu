@@ -133,9 +133,8 @@ BwdLayout bwd_layout(int B, int T, int I, int H, int device, int nclusters) {
   TcGemmArgs hn{nullptr, l.ldh, nullptr, l.ldh, nullptr, H, nullptr, H, H, (int)BT, true, true};
   TcGemmArgs ih{nullptr, l.ldgi, nullptr, l.ldx, nullptr, I, nullptr, 3 * H, I, (int)BT, true, true};
   l.gemm = off;
-  off = align_up(off + std::max({tc_gemm_ws_bytes(hrz, device), tc_gemm_ws_bytes(hn, device),
-                                 tc_gemm_ws_bytes(ih, device)}),
-                 kAlign);
+  const TcGemmArgs grads[3] = {hrz, hn, ih};
+  off = align_up(off + tc_gemm_ws_bytes(grads, 3, device), kAlign);
   // per-cluster FP64 bias-gradient partials written by the backward time loop
   l.col = off;
   off = align_up(off + sizeof(double) * (size_t)nclusters * 4 * H, kAlign);
@@ -250,8 +249,8 @@ int gru_forward(const float* x, const float* h0, const float* w_ih, const float*
   float* wh = reinterpret_cast<float*>(ws + l.wh);
   float* wl = reinterpret_cast<float*>(ws + l.wl);
   // G = x . W_ih^T + b_ih on the tensor cores (3xTF32, pre-split operands).
-  if ((rc = split_tf32(x, (long)B * T, I, I, xh, xl, l.ldx, stream))) return rc;
-  if ((rc = split_tf32(w_ih, 3L * H, I, I, wh, wl, l.ldx, stream))) return rc;
+  const SplitArgs sp[2] = {{x, (long)B * T, I, I, xh, xl, l.ldx}, {w_ih, 3L * H, I, I, wh, wl, l.ldx}};
+  if ((rc = split_tf32_multi(sp, 2, stream))) return rc;
   TcGemmArgs ga{xh, l.ldx, wh, l.ldx, G, l.ldg, b_ih, B * T, 3 * H, I, false, false, xl, wl};
   if ((rc = tc_gemm(ga, stream, kKindInputGemm))) return rc;
   RecGeom g{};
@@ -309,15 +308,15 @@ int gru_backward(const float* dout, const float* dhn, const float* x, const floa
   // dW_hh = dG_hh^T . h_prev (h_prev = stash column block 4), dW_ih = dG_ih^T . x
   // on the tensor cores from pre-split copies.  dW_hh's r/z rows come from
   // dG_ih's r/z columns, its n rows from the separate n block.
-  if ((rc = split_tf32(stash + 4 * H, BT, H, 5L * H, F(l.hph), F(l.hpl), l.ldh, stream))) return rc;
-  if ((rc = split_tf32(x, BT, I, I, F(l.xh), F(l.xl), l.ldx, stream))) return rc;
+  const SplitArgs sp[2] = {{stash + 4 * H, BT, H, 5L * H, F(l.hph), F(l.hpl), l.ldh},
+                           {x, BT, I, I, F(l.xh), F(l.xl), l.ldx}};
+  if ((rc = split_tf32_multi(sp, 2, stream))) return rc;
   TcGemmArgs hrz{F(l.dgih), l.ldgi, F(l.hph), l.ldh, dw_hh, H, nullptr, 2 * H, H, BT, true, true, F(l.dgil), F(l.hpl)};
   TcGemmArgs hn{F(l.dghh), l.ldh, F(l.hph), l.ldh, dw_hh + 2L * H * H, H, nullptr, H, H, BT, true, true, F(l.dghl),
                 F(l.hpl)};
   TcGemmArgs ih{F(l.dgih), l.ldgi, F(l.xh), l.ldx, dw_ih, I, nullptr, H3, I, BT, true, true, F(l.dgil), F(l.xl)};
-  if ((rc = tc_gemm(hrz, stream, kKindGradGemm, gws, gws_bytes))) return rc;
-  if ((rc = tc_gemm(hn, stream, kKindGradGemm, gws, gws_bytes))) return rc;
-  if ((rc = tc_gemm(ih, stream, kKindGradGemm, gws, gws_bytes))) return rc;
+  const TcGemmArgs grads[3] = {hrz, hn, ih};
+  if ((rc = tc_gemm_batch(grads, 3, stream, kKindGradGemm, gws, gws_bytes))) return rc;
   if (dx) {
     // dx = dG_ih . W_ih, with W_ih^T staged (and split) as [I, ldgi].
     if ((rc = transpose(w_ih, H3, I, F(l.wt), l.ldgi, stream))) return rc;

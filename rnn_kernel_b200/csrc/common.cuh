@@ -91,9 +91,25 @@ struct TcGemmArgs {
 // hi[r, c] = tf32(src[r, c]), lo[r, c] = tf32(src - hi) for c < cols, 0 for
 // cols <= c < ldd; src row stride lds, outputs row stride ldd.
 int split_tf32(const float* src, long rows, int cols, long lds, float* hi, float* lo, int ldd, cudaStream_t stream);
+// Several such splits in one launch (1 to 4).
+struct SplitArgs {
+  const float* src;
+  long rows;
+  int cols;
+  long lds;
+  float* hi;
+  float* lo;
+  int ldd;
+};
+int split_tf32_multi(const SplitArgs* a, int n, cudaStream_t stream);
 bool tc_gemm_supported(const TcGemmArgs& a);
 size_t tc_gemm_ws_bytes(const TcGemmArgs& a, int device);
 int tc_gemm(const TcGemmArgs& a, cudaStream_t stream, int kind, void* ws = nullptr, size_t ws_bytes = 0);
+// 1 to 3 products with the same operand majors in ONE launch (a persistent
+// grid over all of their tiles and K splits) plus one launch summing all
+// split-K partials; the workspace holds every product's partials.
+size_t tc_gemm_ws_bytes(const TcGemmArgs* a, int n, int device);
+int tc_gemm_batch(const TcGemmArgs* a, int n, cudaStream_t stream, int kind, void* ws, size_t ws_bytes);
 int read_gemm_status(int reset, int* status);
 
 // Transpose a [rows, cols] matrix into [cols, ldd] (columns rows .. ldd zeroed).

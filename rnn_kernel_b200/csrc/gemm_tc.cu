@@ -26,6 +26,8 @@
 
 #include <cuda.h>
 
+#include <cstring>
+
 #include "common.cuh"
 #include "../../include/rnn_kernel_b200.h"
 
@@ -172,21 +174,42 @@ struct Smem {
 // C + split * M * ldc, without bias, for a later FP64 reduce).  The stage
 // ring, the accumulator pairs and their mbarrier phases continue across units,
 // so loads of the next tile overlap the drain and stores of the previous one.
+//
+// Grouped launch: one kernel runs up to kMaxProblems products (the weight
+// gradients of one backward) as one persistent grid; unit u belongs to the
+// problem whose [unit_begin, unit_end) range holds it.
+constexpr int kMaxProblems = 3;
+struct GemmProblem {
+  CUtensorMap ah, al, bh, bl;  // A hi/lo, B hi/lo tensor maps
+  float* C;
+  long ldc;
+  const float* bias;
+  int M, N, K, kchunk, splits, tiles_n, tiles, unit_end;  // unit_end: cumulative over the batch
+};
+struct GemmBatch {
+  GemmProblem p[kMaxProblems];
+  int np, units;
+};
+
 struct Unit {
-  int m0, n0, kbeg, nk, split;
+  int m0, n0, kbeg, nk, split, pi;
 };
 
 template <int BN>
-__device__ __forceinline__ Unit unit_of(int u, int tiles_n, int tiles, int M, int K, int kchunk) {
+__device__ __forceinline__ Unit unit_of(const GemmBatch& bt, int u) {
   Unit w;
-  const int tile = u % tiles;
-  w.split = u / tiles;
-  w.m0 = (tile / tiles_n) * kBM;
-  w.n0 = (tile % tiles_n) * BN;
-  w.kbeg = w.split * kchunk;
-  const int kend = min(K, w.kbeg + kchunk);
+  int pi = 0;
+  while (pi + 1 < bt.np && u >= bt.p[pi].unit_end) ++pi;
+  const GemmProblem& P = bt.p[pi];
+  const int v = u - (pi > 0 ? bt.p[pi - 1].unit_end : 0);
+  const int tile = v % P.tiles;
+  w.pi = pi;
+  w.split = v / P.tiles;
+  w.m0 = (tile / P.tiles_n) * kBM;
+  w.n0 = (tile % P.tiles_n) * BN;
+  w.kbeg = w.split * P.kchunk;
+  const int kend = min(P.K, w.kbeg + P.kchunk);
   w.nk = kend > w.kbeg ? (kend - w.kbeg + kBK - 1) / kBK : 0;
-  (void)M;
   return w;
 }
 
@@ -206,10 +229,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 
 template <int BN, int S, int NPAIR, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
-gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ah, const __grid_constant__ CUtensorMap map_al,
-                   const __grid_constant__ CUtensorMap map_bh, const __grid_constant__ CUtensorMap map_bl,
-                   float* __restrict__ C, long ldc, const float* __restrict__ bias, int M, int N, int K,
-                   int kchunk, int splits) {
+gemm_tf32x3_kernel(const __grid_constant__ GemmBatch bt) {
   using L = Smem<BN, S>;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled tiles.
@@ -225,9 +245,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ah, const __grid_cons
   constexpr int kCols = 2 * NPAIR * BN;  // tensor-memory columns allocated
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tiles_n = (N + BN - 1) / BN;
-  const int tiles = ((M + kBM - 1) / kBM) * tiles_n;
-  const int units = tiles * splits;
+  const int units = bt.units;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -241,10 +259,12 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ah, const __grid_cons
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0 && lane == 0) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_ah)) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_al)) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_bh)) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_bl)) : "memory");
+    for (int pi = 0; pi < bt.np; ++pi) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&bt.p[pi].ah)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&bt.p[pi].al)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&bt.p[pi].bh)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&bt.p[pi].bl)) : "memory");
+    }
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -262,7 +282,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ah, const __grid_cons
       int i = 0;  // global stage counter of this CTA
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const Unit w = unit_of<BN>(u, tiles_n, tiles, M, K, kchunk);
+        const Unit w = unit_of<BN>(bt, u);
         for (int ks = 0; ks < w.nk; ++ks, ++i) {
           const int s = i % S;
           if (i >= S && !mbar_wait(empty(s), ((i / S) - 1) & 1)) { ok = false; break; }
@@ -270,25 +290,29 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ah, const __grid_cons
           mbar_arrive_expect_tx(full(s), 2 * (L::kATile + L::kBTile));
           const int k0 = w.kbeg + ks * kBK;
           const uint32_t a_hi = st, a_lo = st + L::kATile, b_hi = st + 2 * L::kATile, b_lo = b_hi + L::kBTile;
+          const CUtensorMap* map_ah = &bt.p[w.pi].ah;
+          const CUtensorMap* map_al = &bt.p[w.pi].al;
+          const CUtensorMap* map_bh = &bt.p[w.pi].bh;
+          const CUtensorMap* map_bl = &bt.p[w.pi].bl;
           if (A_MN) {
 #pragma unroll
             for (int j = 0; j < kBM / 32; ++j) {
-              tma_load_2d(a_hi + j * 4096, &map_ah, full(s), w.m0 + 32 * j, k0);
-              tma_load_2d(a_lo + j * 4096, &map_al, full(s), w.m0 + 32 * j, k0);
+              tma_load_2d(a_hi + j * 4096, map_ah, full(s), w.m0 + 32 * j, k0);
+              tma_load_2d(a_lo + j * 4096, map_al, full(s), w.m0 + 32 * j, k0);
             }
           } else {
-            tma_load_2d(a_hi, &map_ah, full(s), k0, w.m0);
-            tma_load_2d(a_lo, &map_al, full(s), k0, w.m0);
+            tma_load_2d(a_hi, map_ah, full(s), k0, w.m0);
+            tma_load_2d(a_lo, map_al, full(s), k0, w.m0);
           }
           if (B_MN) {
 #pragma unroll
             for (int j = 0; j < BN / 32; ++j) {
-              tma_load_2d(b_hi + j * 4096, &map_bh, full(s), w.n0 + 32 * j, k0);
-              tma_load_2d(b_lo + j * 4096, &map_bl, full(s), w.n0 + 32 * j, k0);
+              tma_load_2d(b_hi + j * 4096, map_bh, full(s), w.n0 + 32 * j, k0);
+              tma_load_2d(b_lo + j * 4096, map_bl, full(s), w.n0 + 32 * j, k0);
             }
           } else {
-            tma_load_2d(b_hi, &map_bh, full(s), k0, w.n0);
-            tma_load_2d(b_lo, &map_bl, full(s), k0, w.n0);
+            tma_load_2d(b_hi, map_bh, full(s), k0, w.n0);
+            tma_load_2d(b_lo, map_bl, full(s), k0, w.n0);
           }
         }
       }
@@ -307,7 +331,7 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ah, const __grid_cons
       int i = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const Unit w = unit_of<BN>(u, tiles_n, tiles, M, K, kchunk);
+        const Unit w = unit_of<BN>(bt, u);
         for (int ks = 0; ks < w.nk; ++ks, ++i) {
           const int s = i % S, p = i % NPAIR;
           if (!mbar_wait(full(s), (i / S) & 1)) { ok = false; break; }
@@ -343,10 +367,15 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ah, const __grid_cons
     bool ok = true;
     int d = 0;  // global stage counter of this CTA
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-      const Unit w = unit_of<BN>(u, tiles_n, tiles, M, K, kchunk);
+      const Unit w = unit_of<BN>(bt, u);
       for (int ks = 0; ks < w.nk; ++ks, ++d) {
         const int p = d % NPAIR;
-        if (!mbar_wait(filled(p), (d / NPAIR) & 1)) { ok = false; break; }
+        // one lane polls (32 lanes polling one mbarrier serialise on its
+        // bank), the warp then synchronises before the tensor-memory loads
+        bool got = true;
+        if (lane == 0) got = mbar_wait(filled(p), (d / NPAIR) & 1);
+        got = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
+        if (!got) { ok = false; break; }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
         for (int c0 = 0; c0 < kCW; c0 += 32) {
@@ -362,10 +391,13 @@ gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ah, const __grid_cons
       }
       if (!ok) break;
       // tile finished (units without K work produce a zero tile)
+      const GemmProblem& P = bt.p[w.pi];
+      const int M = P.M, N = P.N;
+      const long ldc = P.ldc;
       const int row = w.m0 + 32 * quarter + lane;
       const int n0 = w.n0 + kCW * chalf;
-      float* Cu = splits > 1 ? C + (long)w.split * M * ldc : C;
-      const float* bu = splits > 1 ? nullptr : bias;
+      float* Cu = P.splits > 1 ? P.C + (long)w.split * M * ldc : P.C;
+      const float* bu = P.splits > 1 ? nullptr : P.bias;
       // Warp-uniform: 16-byte rows, whole 64-column block inside N.
       const bool vec = (ldc % 4 == 0) && n0 + kCW <= N && ((reinterpret_cast<uintptr_t>(Cu + n0) & 15) == 0);
       if (vec) {
@@ -472,22 +504,41 @@ int make_map(CUtensorMap* map, const float* ptr, long rows, long cols, long ld, 
   return GRU_OK;
 }
 
-__global__ void splitk_sum_kernel(const float* __restrict__ part, int S, int M, int N, long ldp,
-                                  float* __restrict__ C, long ldc) {
-  const long MN = (long)M * N;
-  for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < MN; e += (long)gridDim.x * blockDim.x) {
-    const int m = (int)(e / N), n = (int)(e - (long)m * N);
+// Split-K sums of a batch: C_p[m, n] = sum_z part_p[z][m][n] in FP64, for
+// every problem p with splits > 1 (deterministic order).
+struct SplitSum {
+  const float* part;
+  float* C;
+  long ldp, ldc;
+  int S, M, N;
+  long end;  // cumulative element count over the batch
+};
+struct SplitSumBatch {
+  SplitSum q[kMaxProblems];
+  int nq;
+};
+
+__global__ void splitk_sum_kernel(const __grid_constant__ SplitSumBatch sb) {
+  const long total = sb.q[sb.nq - 1].end;
+  for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < total; e += (long)gridDim.x * blockDim.x) {
+    int qi = 0;
+    while (qi + 1 < sb.nq && e >= sb.q[qi].end) ++qi;
+    const SplitSum& Q = sb.q[qi];
+    const long v = e - (qi > 0 ? sb.q[qi - 1].end : 0);
+    const int m = (int)(v / Q.N), n = (int)(v - (long)m * Q.N);
     double acc = 0.0;
-    for (int z = 0; z < S; ++z) acc += part[((long)z * M + m) * ldp + n];
-    C[(long)m * ldc + n] = (float)acc;
+    for (int z = 0; z < Q.S; ++z) acc += Q.part[((long)z * Q.M + m) * Q.ldp + n];
+    Q.C[(long)m * Q.ldc + n] = (float)acc;
   }
 }
 
 constexpr int kBN = 128, kS = 3, kNPAIR = 2;
 using LDefault = Smem<kBN, kS>;
 
+// One launch for problems a[0..n) (same operand majors); problem i writes
+// to C[i] (row stride ldc[i]) with splits[i] K splits of kchunk[i].
 template <bool A_MN, bool B_MN>
-int launch_tc(const TcGemmArgs& a, float* C, long ldc, const float* bias, int splits, int kchunk,
+int launch_tc(const TcGemmArgs* a, int n, float* const* C, const long* ldc, const int* splits, const int* kchunk,
               cudaStream_t stream) {
   auto kern = gemm_tf32x3_kernel<kBN, kS, kNPAIR, A_MN, B_MN>;
   static thread_local int configured_device = -1;
@@ -497,25 +548,43 @@ int launch_tc(const TcGemmArgs& a, float* C, long ldc, const float* bias, int sp
     GRU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, LDefault::kBytes));
     configured_device = dev;
   }
-  CUtensorMap mah, mal, mbh, mbl;
-  int rc;
-  if (A_MN) {
-    if ((rc = make_map(&mah, a.A, a.K, a.M, a.lda, 32, kBK, true))) return rc;
-    if ((rc = make_map(&mal, a.A_lo, a.K, a.M, a.lda, 32, kBK, true))) return rc;
-  } else {
-    if ((rc = make_map(&mah, a.A, a.M, a.K, a.lda, kBK, kBM, false))) return rc;
-    if ((rc = make_map(&mal, a.A_lo, a.M, a.K, a.lda, kBK, kBM, false))) return rc;
+  GemmBatch bt;
+  memset(&bt, 0, sizeof(bt));
+  bt.np = n;
+  int units = 0;
+  for (int i = 0; i < n; ++i) {
+    GemmProblem& P = bt.p[i];
+    int rc;
+    if (A_MN) {
+      if ((rc = make_map(&P.ah, a[i].A, a[i].K, a[i].M, a[i].lda, 32, kBK, true))) return rc;
+      if ((rc = make_map(&P.al, a[i].A_lo, a[i].K, a[i].M, a[i].lda, 32, kBK, true))) return rc;
+    } else {
+      if ((rc = make_map(&P.ah, a[i].A, a[i].M, a[i].K, a[i].lda, kBK, kBM, false))) return rc;
+      if ((rc = make_map(&P.al, a[i].A_lo, a[i].M, a[i].K, a[i].lda, kBK, kBM, false))) return rc;
+    }
+    if (B_MN) {
+      if ((rc = make_map(&P.bh, a[i].B, a[i].K, a[i].N, a[i].ldb, 32, kBK, true))) return rc;
+      if ((rc = make_map(&P.bl, a[i].B_lo, a[i].K, a[i].N, a[i].ldb, 32, kBK, true))) return rc;
+    } else {
+      if ((rc = make_map(&P.bh, a[i].B, a[i].N, a[i].K, a[i].ldb, kBK, kBN, false))) return rc;
+      if ((rc = make_map(&P.bl, a[i].B_lo, a[i].N, a[i].K, a[i].ldb, kBK, kBN, false))) return rc;
+    }
+    P.C = C[i];
+    P.ldc = ldc[i];
+    P.bias = splits[i] > 1 ? nullptr : a[i].bias;
+    P.M = a[i].M;
+    P.N = a[i].N;
+    P.K = a[i].K;
+    P.kchunk = kchunk[i];
+    P.splits = splits[i];
+    P.tiles_n = (a[i].N + kBN - 1) / kBN;
+    P.tiles = ((a[i].M + kBM - 1) / kBM) * P.tiles_n;
+    units += P.tiles * splits[i];
+    P.unit_end = units;
   }
-  if (B_MN) {
-    if ((rc = make_map(&mbh, a.B, a.K, a.N, a.ldb, 32, kBK, true))) return rc;
-    if ((rc = make_map(&mbl, a.B_lo, a.K, a.N, a.ldb, 32, kBK, true))) return rc;
-  } else {
-    if ((rc = make_map(&mbh, a.B, a.N, a.K, a.ldb, kBK, kBN, false))) return rc;
-    if ((rc = make_map(&mbl, a.B_lo, a.N, a.K, a.ldb, kBK, kBN, false))) return rc;
-  }
-  const int units = ((a.M + kBM - 1) / kBM) * ((a.N + kBN - 1) / kBN) * splits;
+  bt.units = units;
   const int grid = units < sm_count(dev) ? units : sm_count(dev);
-  kern<<<grid, kThreads, LDefault::kBytes, stream>>>(mah, mal, mbh, mbl, C, ldc, bias, a.M, a.N, a.K, kchunk, splits);
+  kern<<<grid, kThreads, LDefault::kBytes, stream>>>(bt);
   GRU_CUDA_TRY(cudaGetLastError());
   return GRU_OK;
 }
@@ -527,25 +596,43 @@ __device__ __forceinline__ void split4(float4 v, float4& h, float4& l) {
                   __uint_as_float(to_tf32(v.z - h.z)), __uint_as_float(to_tf32(v.w - h.w)));
 }
 
-// One row per (blockIdx.x + k * gridDim.x), threads across the columns;
-// float4 when the source rows allow it (vec), else scalar.
-__global__ void split_tf32_kernel(const float* __restrict__ src, long rows, int cols, long lds,
-                                  float* __restrict__ hi, float* __restrict__ lo, int ldd, bool vec) {
-  for (long r = blockIdx.x; r < rows; r += gridDim.x) {
-    const float* sr = src + r * lds;
-    float* hr = hi + r * ldd;
-    float* lr = lo + r * ldd;
-    if (vec) {
-      for (int c = 4 * threadIdx.x; c < ldd; c += 4 * blockDim.x) {
-        const float4 v = c < cols ? *reinterpret_cast<const float4*>(sr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+// One split job: hi[r, c] = tf32(src[r, c]), lo[r, c] = tf32(src - hi) for
+// c < cols, 0 for cols <= c < ldd.
+struct SplitJob {
+  const float* src;
+  float* hi;
+  float* lo;
+  long rows, lds, row_end;  // row_end: cumulative rows over the launch
+  int cols, ldd, vec;       // vec: float4 path allowed
+};
+struct SplitJobs {
+  SplitJob j[4];
+  int n;
+};
+
+// One row per (blockIdx.x + k * gridDim.x) over the rows of all jobs,
+// threads across the columns; float4 when the job's rows allow it.
+__global__ void split_tf32_kernel(const __grid_constant__ SplitJobs js) {
+  const long total = js.j[js.n - 1].row_end;
+  for (long g = blockIdx.x; g < total; g += gridDim.x) {
+    int ji = 0;
+    while (ji + 1 < js.n && g >= js.j[ji].row_end) ++ji;
+    const SplitJob& J = js.j[ji];
+    const long r = g - (ji > 0 ? js.j[ji - 1].row_end : 0);
+    const float* sr = J.src + r * J.lds;
+    float* hr = J.hi + r * J.ldd;
+    float* lr = J.lo + r * J.ldd;
+    if (J.vec) {
+      for (int c = 4 * threadIdx.x; c < J.ldd; c += 4 * blockDim.x) {
+        const float4 v = c < J.cols ? *reinterpret_cast<const float4*>(sr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
         float4 h, l;
         split4(v, h, l);
         *reinterpret_cast<float4*>(hr + c) = h;
         *reinterpret_cast<float4*>(lr + c) = l;
       }
     } else {
-      for (int c = threadIdx.x; c < ldd; c += blockDim.x) {
-        const float v = c < cols ? sr[c] : 0.0f;
+      for (int c = threadIdx.x; c < J.ldd; c += blockDim.x) {
+        const float v = c < J.cols ? sr[c] : 0.0f;
         const uint32_t h = to_tf32(v);
         hr[c] = __uint_as_float(h);
         lr[c] = __uint_as_float(to_tf32(v - __uint_as_float(h)));
@@ -556,17 +643,44 @@ __global__ void split_tf32_kernel(const float* __restrict__ src, long rows, int 
 
 }  // namespace
 
-int split_tf32(const float* src, long rows, int cols, long lds, float* hi, float* lo, int ldd, cudaStream_t stream) {
-  if (rows <= 0) return GRU_OK;
-  const bool vec = cols % 4 == 0 && lds % 4 == 0 && ldd % 4 == 0 &&
-                   ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(hi) |
-                     reinterpret_cast<uintptr_t>(lo)) & 15) == 0;
-  const int threads = ldd >= 1024 ? 256 : (ldd >= 256 ? 64 : 32);
+int split_tf32_multi(const SplitArgs* a, int n, cudaStream_t stream) {
+  if (n < 1 || n > 4) {
+    set_error("split_tf32: 1 to 4 jobs per launch");
+    return GRU_ERR_INVALID;
+  }
+  SplitJobs js;
+  memset(&js, 0, sizeof(js));
+  long rows = 0;
+  int maxld = 0;
+  for (int i = 0; i < n; ++i) {
+    if (a[i].rows <= 0) continue;
+    SplitJob& J = js.j[js.n++];
+    J.src = a[i].src;
+    J.hi = a[i].hi;
+    J.lo = a[i].lo;
+    J.rows = a[i].rows;
+    J.lds = a[i].lds;
+    J.cols = a[i].cols;
+    J.ldd = a[i].ldd;
+    J.vec = (a[i].cols % 4 == 0 && a[i].lds % 4 == 0 && a[i].ldd % 4 == 0 &&
+             ((reinterpret_cast<uintptr_t>(a[i].src) | reinterpret_cast<uintptr_t>(a[i].hi) |
+               reinterpret_cast<uintptr_t>(a[i].lo)) & 15) == 0) ? 1 : 0;
+    rows += a[i].rows;
+    J.row_end = rows;
+    if (a[i].ldd > maxld) maxld = a[i].ldd;
+  }
+  if (js.n == 0) return GRU_OK;
+  const int threads = maxld >= 1024 ? 256 : (maxld >= 256 ? 64 : 32);
   const long blocks = rows < 16384 ? rows : 16384;
   LaunchScope scope(kKindLayout, stream);
-  split_tf32_kernel<<<(unsigned)blocks, threads, 0, stream>>>(src, rows, cols, lds, hi, lo, ldd, vec);
+  split_tf32_kernel<<<(unsigned)blocks, threads, 0, stream>>>(js);
   GRU_CUDA_TRY(cudaGetLastError());
   return GRU_OK;
+}
+
+int split_tf32(const float* src, long rows, int cols, long lds, float* hi, float* lo, int ldd, cudaStream_t stream) {
+  const SplitArgs a{src, rows, cols, lds, hi, lo, ldd};
+  return split_tf32_multi(&a, 1, stream);
 }
 
 int read_gemm_status(int reset, int* status) {
@@ -584,60 +698,122 @@ bool tc_gemm_supported(const TcGemmArgs& a) {
          a.lda % 4 == 0 && a.ldb % 4 == 0 && a.K >= 1;
 }
 
-int tc_splits(const TcGemmArgs& a, int device) {
-  // Long K (the weight gradients, K = B*T) with few output tiles: split K so
-  // the grid covers the SMs about twice, keeping >= 8 K stages per split.
-  const int tiles = ((a.M + kBM - 1) / kBM) * ((a.N + kBN - 1) / kBN);
-  const int stages = (a.K + kBK - 1) / kBK;
-  int s = (2 * sm_count(device) + tiles - 1) / tiles;
-  if (s > stages / 8) s = stages / 8;
-  return s < 1 ? 1 : s;
+// K splits of the products of one launch: long K (the weight gradients,
+// K = B*T) with few output tiles is split so that the whole batch covers the
+// SMs about twice, each problem's share in proportion to its work, keeping
+// >= 8 K stages per split.  Without a workspace nothing is split.
+void tc_splits(const TcGemmArgs* a, int n, int device, int* out) {
+  long work = 0;
+  for (int i = 0; i < n; ++i)
+    work += (long)((a[i].M + kBM - 1) / kBM) * ((a[i].N + kBN - 1) / kBN) * ((a[i].K + kBK - 1) / kBK);
+  for (int i = 0; i < n; ++i) {
+    const int tiles = ((a[i].M + kBM - 1) / kBM) * ((a[i].N + kBN - 1) / kBN);
+    const int stages = (a[i].K + kBK - 1) / kBK;
+    const double share = work > 0 ? (double)tiles * stages / (double)work : 1.0;
+    int s = (int)(2.0 * sm_count(device) * share / tiles + 0.5);
+    if (s > stages / 8) s = stages / 8;
+    out[i] = s < 1 ? 1 : s;
+  }
 }
 
-size_t tc_gemm_ws_bytes(const TcGemmArgs& a, int device) {
-  const int s = tc_splits(a, device);
+size_t tc_gemm_ws_bytes(const TcGemmArgs* a, int n, int device) {
+  int sp[kMaxProblems];
+  tc_splits(a, n, device, sp);
+  size_t total = 0;
   // partials [s][M][N rounded up to 4 floats]: 16-byte rows for the epilogue
-  return s > 1 ? sizeof(float) * (size_t)s * a.M * ((a.N + 3) / 4 * 4) : 0;
+  for (int i = 0; i < n; ++i)
+    if (sp[i] > 1) total += align_up(sizeof(float) * (size_t)sp[i] * a[i].M * ((a[i].N + 3) / 4 * 4), 256);
+  return total;
 }
 
-int tc_gemm(const TcGemmArgs& a, cudaStream_t stream, int kind, void* ws, size_t ws_bytes) {
-  if (a.M <= 0 || a.N <= 0) return GRU_OK;
-  if (!tc_gemm_supported(a)) {
-    set_error("tc_gemm: operands must be pre-split (hi and lo), 16-byte aligned, with row strides a multiple of 4 floats");
+size_t tc_gemm_ws_bytes(const TcGemmArgs& a, int device) { return tc_gemm_ws_bytes(&a, 1, device); }
+
+int tc_gemm_batch(const TcGemmArgs* a, int n, cudaStream_t stream, int kind, void* ws, size_t ws_bytes) {
+  if (n < 1 || n > kMaxProblems) {
+    set_error("tc_gemm: 1 to 3 products per launch");
     return GRU_ERR_INVALID;
   }
   int dev = 0;
   GRU_CUDA_TRY(cudaGetDevice(&dev));
-  const int splits = ws ? tc_splits(a, dev) : 1;
-  const int kchunk = splits > 1 ? ((a.K + splits * kBK - 1) / (splits * kBK)) * kBK : a.K;
-  float* C = a.C;
-  long ldc = a.ldc;
-  if (splits > 1) {
-    if (ws_bytes < tc_gemm_ws_bytes(a, dev)) {
+  int sp[kMaxProblems], kc[kMaxProblems];
+  float* C[kMaxProblems];
+  long ldc[kMaxProblems];
+  if (ws) {
+    tc_splits(a, n, dev, sp);
+    if (ws_bytes < tc_gemm_ws_bytes(a, n, dev)) {
       set_error("tc_gemm: split-K workspace too small");
       return GRU_ERR_INVALID;
     }
-    C = static_cast<float*>(ws);
-    ldc = (a.N + 3) / 4 * 4;
+  } else {
+    for (int i = 0; i < n; ++i) sp[i] = 1;
   }
-  LaunchScope scope(kind, stream, splits > 1 ? 2 : 1);
+  SplitSumBatch sb;
+  memset(&sb, 0, sizeof(sb));
+  char* wp = static_cast<char*>(ws);
+  long sum_elems = 0;
+  int live = 0;  // problems with something to compute
+  TcGemmArgs run[kMaxProblems];
+  int rsp[kMaxProblems], rkc[kMaxProblems];
+  float* rC[kMaxProblems];
+  long rldc[kMaxProblems];
+  for (int i = 0; i < n; ++i) {
+    if (a[i].M <= 0 || a[i].N <= 0) continue;
+    if (!tc_gemm_supported(a[i])) {
+      set_error("tc_gemm: operands must be pre-split (hi and lo), 16-byte aligned, with row strides a multiple of 4 floats");
+      return GRU_ERR_INVALID;
+    }
+    if (a[i].a_mn != a[0].a_mn || a[i].b_mn != a[0].b_mn) {
+      set_error("tc_gemm: the products of one launch must share their operand majors");
+      return GRU_ERR_INVALID;
+    }
+    kc[i] = sp[i] > 1 ? ((a[i].K + sp[i] * kBK - 1) / (sp[i] * kBK)) * kBK : a[i].K;
+    C[i] = a[i].C;
+    ldc[i] = a[i].ldc;
+    if (sp[i] > 1) {
+      if (a[i].bias) {
+        set_error("tc_gemm: bias with split-K is not supported");
+        return GRU_ERR_INVALID;
+      }
+      C[i] = reinterpret_cast<float*>(wp);
+      ldc[i] = (a[i].N + 3) / 4 * 4;
+      wp += align_up(sizeof(float) * (size_t)sp[i] * a[i].M * ldc[i], 256);
+      SplitSum& Q = sb.q[sb.nq++];
+      Q.part = C[i];
+      Q.C = a[i].C;
+      Q.ldp = ldc[i];
+      Q.ldc = a[i].ldc;
+      Q.S = sp[i];
+      Q.M = a[i].M;
+      Q.N = a[i].N;
+      sum_elems += (long)a[i].M * a[i].N;
+      Q.end = sum_elems;
+    }
+    run[live] = a[i];
+    rsp[live] = sp[i];
+    rkc[live] = kc[i];
+    rC[live] = C[i];
+    rldc[live] = ldc[i];
+    ++live;
+  }
+  if (live == 0) return GRU_OK;
+  LaunchScope scope(kind, stream, sb.nq > 0 ? 2 : 1);
   int rc;
-  if (a.a_mn && a.b_mn) rc = launch_tc<true, true>(a, C, ldc, a.bias, splits, kchunk, stream);
-  else if (!a.a_mn && !a.b_mn) rc = launch_tc<false, false>(a, C, ldc, a.bias, splits, kchunk, stream);
+  if (run[0].a_mn && run[0].b_mn) rc = launch_tc<true, true>(run, live, rC, rldc, rsp, rkc, stream);
+  else if (!run[0].a_mn && !run[0].b_mn) rc = launch_tc<false, false>(run, live, rC, rldc, rsp, rkc, stream);
   else {
     set_error("tc_gemm: mixed operand majors are not instantiated");
     return GRU_ERR_INVALID;
   }
   if (rc) return rc;
-  if (splits > 1) {
-    if (a.bias) {
-      set_error("tc_gemm: bias with split-K is not supported");
-      return GRU_ERR_INVALID;
-    }
-    splitk_sum_kernel<<<sm_count(dev) * 4, 256, 0, stream>>>(C, splits, a.M, a.N, ldc, a.C, a.ldc);
+  if (sb.nq > 0) {
+    splitk_sum_kernel<<<sm_count(dev) * 4, 256, 0, stream>>>(sb);
     GRU_CUDA_TRY(cudaGetLastError());
   }
   return GRU_OK;
+}
+
+int tc_gemm(const TcGemmArgs& a, cudaStream_t stream, int kind, void* ws, size_t ws_bytes) {
+  return tc_gemm_batch(&a, 1, stream, kind, ws, ws_bytes);
 }
 
 }  // namespace gru
