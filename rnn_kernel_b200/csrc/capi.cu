@@ -104,7 +104,7 @@ struct BwdLayout {
   int ldx;   // row stride of the split x copy (I rounded up to 4)
 };
 
-BwdLayout bwd_layout(int B, int T, int I, int H, int device, int nclusters) {
+BwdLayout bwd_layout(int B, int T, int I, int H, int device) {
   const long BT = (long)B * T;
   BwdLayout l{};
   l.ldgi = pad4(3 * H);
@@ -135,9 +135,10 @@ BwdLayout bwd_layout(int B, int T, int I, int H, int device, int nclusters) {
   l.gemm = off;
   const TcGemmArgs grads[3] = {hrz, hn, ih};
   off = align_up(off + tc_gemm_ws_bytes(grads, 3, device), kAlign);
-  // per-cluster FP64 bias-gradient partials written by the backward time loop
+  // per-cluster FP64 bias-gradient partials written by the backward time loop,
+  // sized for B clusters (an upper bound that needs no device query)
   l.col = off;
-  off = align_up(off + sizeof(double) * (size_t)nclusters * 4 * H, kAlign);
+  off = align_up(off + sizeof(double) * (size_t)B * 4 * H, kAlign);
   l.total = off;
   return l;
 }
@@ -213,9 +214,7 @@ size_t gru_backward_workspace_bytes(int B, int T, int I, int H) {
     cudaGetLastError();
     dev = 0;
   }
-  RecGeom g{};
-  if (geometry(1, B, T, H, dev, &g) != GRU_OK) return 0;
-  return bwd_layout(B, T, I, H, dev, g.nclusters).total;
+  return bwd_layout(B, T, I, H, dev).total;
 }
 
 int gru_forward(const float* x, const float* h0, const float* w_ih, const float* w_hh,
@@ -289,7 +288,7 @@ int gru_backward(const float* dout, const float* dhn, const float* x, const floa
   }
   RecGeom g{};
   if ((rc = geometry(1, B, T, H, dev, &g))) return rc;
-  const BwdLayout l = bwd_layout(B, T, I, H, dev, g.nclusters);
+  const BwdLayout l = bwd_layout(B, T, I, H, dev);
   if (!workspace || workspace_bytes < l.total) {
     set_error("gru_backward: workspace too small");
     return GRU_ERR_INVALID;
