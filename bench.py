@@ -24,7 +24,8 @@ Beside the headline the line carries
 Rank 0 prints one JSON line.  Timing: W untimed warm-up steps, then exactly K
 steps, each bracketed by CUDA events on the launching stream, with a 256 MiB
 L2 flush between steps outside the events; barrier + synchronize on both
-sides; per-step statistics are the max over ranks.
+sides; per-step statistics are the max over ranks.  A ~30 ms device sleep
+before the first timed step lets the host enqueue ahead of the GPU.
 """
 from __future__ import annotations
 
@@ -262,7 +263,13 @@ def load_traffic():
 # timing helpers
 # ---------------------------------------------------------------------------
 def timed_steps(step_fn, K, flush, torch):
+    """Per-step device times (ms).  A device-side sleep first lets the host
+    enqueue the K steps ahead of the GPU, so a host-side stall while
+    launching (seen at 8 ranks: one step in 20 waiting 10-18 ms for its
+    launches) does not leave the GPU idle inside a step's event window; the
+    sleep itself is outside every window."""
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    torch.cuda._sleep(int(30e-3 * 1.965e9))  # ~30 ms of device cycles
     for k in range(K):
         flush()
         evs[k][0].record()
