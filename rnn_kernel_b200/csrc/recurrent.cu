@@ -797,6 +797,23 @@ const void* kernel_for(bool fwd, int R) {
   }
 }
 
+// Rows per sub-chunk for bc rows per cluster, hcnt units per CTA and nthr
+// threads: at most kMaxRows, balanced across the sub-chunks (e.g. 5 + 4
+// instead of 8 + 1 rows: every sub-chunk costs about one step's latency
+// whatever its rows; I=H=256, B=128: both time loops 20 % faster) as long as
+// the last sub-chunk leaves enough threads without a pointwise item: those
+// threads issue the next steps' input prefetch, and too few of them made it
+// the bottleneck (35 rows balanced as 5 x 7 at H=256: backward 14.5 ->
+// 23.5 ms).  Enough = 64 for the forward (3 inputs per item), 128 for the
+// backward (6 inputs; 18 rows as 3 x 6 with 64 idle: 4.2 -> 4.9 ms).
+inline int rows_per_subchunk(int bc, int hcnt, int nthr, bool fwd) {
+  if (bc <= kMaxRows) return bc;
+  const int nsub = ceil_div(bc, kMaxRows);
+  const int rb = ceil_div(bc, nsub);
+  const int last = bc - (nsub - 1) * rb;
+  return nthr - last * hcnt >= (fwd ? 64 : 128) ? rb : kMaxRows;
+}
+
 // Choose the batch rows per cluster: spread B over as many clusters as can be
 // resident at once, subject to the shared-memory budget.
 template <typename SmemFn>
@@ -839,7 +856,7 @@ int finish_geometry(RecGeom* g, int device, bool fwd, SmemFn smem_of) {
   int bc = ceil_div(g->B, max_clusters);
   for (;;) {
     g->bc = bc;
-    g->R = bc < kMaxRows ? bc : kMaxRows;
+    g->R = rows_per_subchunk(bc, g->Hc, 32 * g->nw, fwd);
     g->bcp = ceil_div(bc, g->R) * g->R;
     g->pd = kMaxPrefetch;  // prefetch issued at the end of step t for step t + pd - 1
     while (g->pd > 2 && smem_of(*g) > (size_t)max_smem) --g->pd;
@@ -857,7 +874,7 @@ int finish_geometry(RecGeom* g, int device, bool fwd, SmemFn smem_of) {
     // whole waves (narrower clusters, each step cheaper).
     const int waves = ceil_div(g->nclusters, max_clusters);
     g->bc = ceil_div(g->B, waves * max_clusters);
-    g->R = g->bc < kMaxRows ? g->bc : kMaxRows;
+    g->R = rows_per_subchunk(g->bc, g->Hc, 32 * g->nw, fwd);
     g->bcp = ceil_div(g->bc, g->R) * g->R;
     g->pd = kMaxPrefetch;
     while (g->pd > 2 && smem_of(*g) > (size_t)max_smem) --g->pd;
