@@ -269,7 +269,9 @@ def timed_steps(step_fn, K, flush, torch):
     launches) does not leave the GPU idle inside a step's event window; the
     sleep itself is outside every window."""
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
-    torch.cuda._sleep(int(30e-3 * 1.965e9))  # ~30 ms of device cycles
+    sleep = getattr(torch.cuda, "_sleep", None)
+    if sleep is not None:
+        sleep(int(30e-3 * 1.965e9))  # ~30 ms of device cycles
     for k in range(K):
         flush()
         evs[k][0].record()

@@ -177,6 +177,9 @@ class GraphedTrainStep:
 
     def __init__(self, trainer: DataParallelTrainer, inputs, warmup: int = 3,
                  capture_error_mode: str = "global", include_update: bool = False) -> None:
+        if include_update and trainer.world > 1:
+            raise ValueError("GraphedTrainStep(include_update=True) is for a single process: keep the NCCL "
+                             "all-reduce eager with a process group")
         self.trainer = trainer
         self.include_update = include_update
         trainer.overlap_active = False
