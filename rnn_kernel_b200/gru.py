@@ -6,7 +6,8 @@ Mirrors the reference's prod surface (``src/rnn_kernel/a100/prod/gru.py``):
   (output [B,T,H], h_n [1,B,H])`` with backward returning ``(dx, dh0, dW_ih,
   dW_hh, db_ih, db_hh)`` (ref ``_A100GRUFunction``, ``:488-580``);
 * :class:`GRU` — the ``nn.Module`` (ref ``A100GRU``, ``:620-786``) with
-  ``forward(x, hx=None) -> (output, h_n [L,B,H])``, ``forward_inference`` and
+  ``forward(x, hx=None) -> (output, h_n [L,B,H])``, ``forward_inference``,
+  ``forward_output_only`` and
   the automatic no-stash path under ``torch.no_grad()`` (``:761-778``);
 * :func:`from_torch_gru`, :func:`is_supported_gru`, :func:`is_b200_available`
   (ref ``from_torch_gru`` ``:789-808``, ``is_supported_gru`` ``:120-136``,
@@ -256,6 +257,14 @@ class GRU(nn.Module):
         """Explicit forward-only, no-stash path."""
         hx = self._prepare_hx(x, hx)
         return self._run(x, hx, train=False)
+
+    def forward_output_only(self, x: torch.Tensor, hx: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """``output`` only, for callers that never use ``h_n`` (the reference
+        harness's ``use_a100_output_only`` path, ``rnn_benchmark.py:521-522``;
+        ref ``A100GRUH256.forward_output_only``, ``gru_autograd.py:5768-5777``).
+        Trains through autograd when grad is enabled, else takes the no-stash
+        path."""
+        return self.forward(x, hx)[0]
 
     @classmethod
     def from_torch_gru(cls, gru: nn.GRU) -> "GRU":

@@ -1,4 +1,6 @@
 """GPU parity of the B200 GRU against torch.nn.GRU FP32 (and the fixtures)."""
+import copy
+
 import numpy as np
 import pytest
 import torch
@@ -124,6 +126,34 @@ def test_inference_paths_match(L):
     for o, h in ((o1, h1), (o2, h2)):
         torch.testing.assert_close(o.cpu(), r_out, rtol=RTOL, atol=ATOL)
         torch.testing.assert_close(h.cpu(), r_hn, rtol=RTOL, atol=ATOL)
+
+
+@pytest.mark.parametrize("L", [2, 3])
+def test_forward_output_only_matches_torch(L):
+    # mirrors tests/test_a100_gru_autograd.py:194-228 (h_n unused), at the
+    # north-star tolerance against torch float64
+    torch.manual_seed(2180 + L)
+    ref = torch.nn.GRU(16, 256, num_layers=L, batch_first=True)
+    m = from_torch_gru(copy.deepcopy(ref).cuda())
+    ref = ref.double()
+    x = torch.randn(2, 5, 16, dtype=torch.float64)
+    h0 = torch.randn(L, 2, 256, dtype=torch.float64)
+    go = torch.randn(2, 5, 256, dtype=torch.float64)
+    xr, hr = x.clone().requires_grad_(True), h0.clone().requires_grad_(True)
+    out_r, _ = ref(xr, hr)
+    out_r.backward(go)
+    xm = x.float().cuda().requires_grad_(True)
+    hm = h0.float().cuda().requires_grad_(True)
+    out_m = m.forward_output_only(xm, hm)
+    out_m.backward(go.float().cuda())
+    torch.testing.assert_close(out_m.double().cpu(), out_r.detach(), rtol=RTOL, atol=ATOL)
+    torch.testing.assert_close(xm.grad.double().cpu(), xr.grad, rtol=RTOL, atol=ATOL)
+    torch.testing.assert_close(hm.grad.double().cpu(), hr.grad, rtol=RTOL, atol=ATOL)
+    for name, p in ref.named_parameters():
+        torch.testing.assert_close(getattr(m, name).grad.double().cpu(), p.grad, rtol=RTOL, atol=ATOL)
+    with torch.no_grad():
+        o = m.forward_output_only(xm)
+    assert o.shape == (2, 5, 256) and not o.requires_grad
 
 
 def test_sequence_chunking_matches_full_bptt():
