@@ -254,7 +254,7 @@ gemm_tf32x3_kernel(const __grid_constant__ GemmBatch bt) {
     }
     for (int p = 0; p < NPAIR; ++p) {
       mbar_init(filled(p), 1);
-      mbar_init(drained(p), 32 * kDrainWarps);
+      mbar_init(drained(p), kDrainWarps);  // one arrival per drain warp
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -387,7 +387,8 @@ gemm_tf32x3_kernel(const __grid_constant__ GemmBatch bt) {
           for (int jj = 0; jj < 32; ++jj) acc[c0 + jj] += __uint_as_float(rb[jj]) + __uint_as_float(rs[jj]);
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        mbar_arrive(drained(p));
+        __syncwarp();  // every lane's tensor-memory loads of this pair are done
+        if (lane == 0) mbar_arrive(drained(p));
       }
       if (!ok) break;
       // tile finished (units without K work produce a zero tile)
