@@ -66,6 +66,8 @@ def parse():
     ap.add_argument("--no-dp-check", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the cuDNN comparison sweep")
     ap.add_argument("--no-graph", action="store_true", help="eager steps only (no CUDA graph replay)")
+    ap.add_argument("--time-chunks", type=int, default=0,
+                    help="time chunks of the forward/backward (0 automatic, 1 off, 2..4 forced where possible)")
     return ap.parse_args()
 
 
@@ -458,6 +460,7 @@ def main():
 
     from rnn_kernel_b200 import GRU, DataParallelTrainer, GraphedTrainStep, _lib
 
+    _lib.set_time_chunks(args.time_chunks)
     B = args.global_batch // world if args.global_batch else args.batch_per_gpu
     T, I, H, L = args.seq_len, args.input_size, args.hidden_size, args.layers
     K, W = args.steps, max(3, args.warmup)
@@ -619,7 +622,10 @@ def main():
                 for k, (tot, n) in ktimes.items()}
     dom = max(("fwd_recurrent", "bwd_recurrent"), key=lambda k: ktimes[k][0])
     dom_ms = per_kind[dom]["ms_per_launch"]
-    flops = recurrent_flops(B, T, H, dom == "bwd_recurrent")
+    # with time chunks a layer's pass over the sequence is several launches,
+    # each over T / chunks steps
+    chunks = max(1, round(ktimes[dom][1] / (K * L))) if ktimes[dom][1] else 1
+    flops = recurrent_flops(B, T, H, dom == "bwd_recurrent") / chunks
     achieved = flops / (dom_ms / 1e3) / 1e12 if dom_ms else None
     peak = fp32_peak_tflops(1965.0)
     roofline = {
@@ -630,7 +636,8 @@ def main():
         "peak_source": "nominal FP32 CUDA-core peak 148 SM x 128 FMA/clk x 2 x 1965 MHz "
                        "(MEASURED_PEAKS.json has HBM and bf16 tensor figures only)",
         "flops_per_launch": flops,
-        "us_per_timestep": dom_ms * 1e3 / T if dom_ms else None,
+        "launches_per_pass": chunks,
+        "us_per_timestep": dom_ms * 1e3 / (T / chunks) if dom_ms else None,
     }
     t_roof = step_roofline_ms(B, T, H, 1965.0) * L
     # Side-by-side bounds: + the step's tensor-core products at 3xTF32
@@ -662,7 +669,8 @@ def main():
         "config": {"workload": f"gru_train_step {L}-layer I={I} H={H} T={T}, batch {B}/GPU "
                                f"(fwd + MSE + bwd + allreduce + SGD lr 1e-2)",
                    "global_batch": B * world, "seq_len": T, "input_size": I, "hidden_size": H, "layers": L,
-                   "parallelism": f"dp{world}", "l2": "256 MiB flush between timed steps (outside the events)"},
+                   "parallelism": f"dp{world}", "l2": "256 MiB flush between timed steps (outside the events)",
+                   "time_chunks": args.time_chunks},
         "clocks": clocks,
         "gpu_launches": int(launches),
         "kernels": per_kind,

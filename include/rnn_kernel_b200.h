@@ -100,6 +100,19 @@ int gru_forward_inference_noalloc(const float* x, const float* h0, const float* 
                                   const float* w_hh, const float* b_ih, const float* b_hh,
                                   float* out, float* hn, int B, int T, int I, int H, void* stream);
 
+/* Time chunks (no reference counterpart; a scheduling knob of this library).
+ * When the time loops leave SMs idle (e.g. 104 of 148 at H = 256, B = 64),
+ * gru_forward and gru_backward run the sequence as n consecutive chunks and
+ * put the tensor-core products of one chunk on the idle SMs (an internal
+ * side stream, joined before the call returns) beside the loop over another.
+ * n = 0: automatic (2 chunks when T is a multiple of 256 and a cost
+ * estimate says the overlap pays for the extra loop launch); 1: off; 2..4:
+ * that many chunks whenever T is a multiple of 128 * n, the loop is one wave
+ * and leaves an SM idle.  Results are the same up to the order of
+ * the weight-gradient partial sums.  Process-wide; returns the previous
+ * setting, or -1 for an invalid n. */
+int gru_set_time_chunks(int n);
+
 /* ---- Telemetry (no reference counterpart: the reference had no kernel
  * timers; its profiling scripts used torch.profiler / nsys, see
  * scripts/profile_a100_h256_step.py).  Kernel kinds: 0 input-projection GEMM,

@@ -38,6 +38,7 @@ SIGNATURES = {
     "gru_device_status": (_int, [_int]),
     "gru_selftest_wait_timeout": (_int, [_int, ctypes.c_void_p, ctypes.c_void_p]),
     "gru_launch_count": (ctypes.c_ulonglong, []),
+    "gru_set_time_chunks": (_int, [_int]),
     "gru_timing_enable": (_int, [_int]),
     "gru_timing_collect": (_int, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int), _int]),
 }
@@ -64,6 +65,15 @@ def device_status(reset: bool = False) -> int:
     if st < 0:
         raise RuntimeError(f"gru_device_status failed: {last_error()}")
     return st
+
+
+def set_time_chunks(n: int) -> int:
+    """Time chunks of the forward/backward (0 automatic, 1 off, 2..4 forced
+    where the shape allows); returns the previous setting."""
+    prev = load().gru_set_time_chunks(int(n))
+    if prev < 0:
+        raise ValueError(f"time chunks must be 0..4, got {n}")
+    return prev
 
 
 def launch_count() -> int:

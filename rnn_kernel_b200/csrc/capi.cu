@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <string>
@@ -21,6 +22,79 @@ std::map<std::tuple<int, int, int, int>, RecGeom> g_geom;  // (device, kind, B, 
 std::map<int, int> g_sms;
 
 constexpr size_t kAlign = 256;
+
+// Time chunks.  The time loops occupy C * nclusters SMs (e.g. 104 of 148 at
+// H = 256, B = 64), so while one chunk of the sequence runs, the tensor-core
+// products of another chunk run on the idle SMs from a side stream: in the
+// forward the input projection of chunk c+1 beside the loop over chunk c, in
+// the backward the weight-gradient (and dx) products of chunk c beside the
+// loop over chunk c-1.  A chunk is a multiple of 128 steps (whole M tiles of
+// the projection per batch row).
+constexpr int kMaxChunks = 4;
+std::atomic<int> g_time_chunks{0};  // 0: automatic, 1: off, 2..kMaxChunks: that many when possible
+
+// Automatic choice (two chunks or none) from a cost estimate: the chunked
+// run saves the tensor-core time of one half of the products on the whole
+// GPU, loses whatever the side half takes beyond the loop over the other
+// half, and pays one more loop launch (measured ~15-30 us: prologue and
+// pipeline fill).  Rates are conservative measurements at I = H = 256: the
+// 3xTF32 products ~0.7 TFLOP/s (FP32-equivalent) per SM, a time-loop step
+// ~1.6 us per GEMV sub-chunk of <= 8 rows.
+constexpr double kGemmFlopsPerSm = 0.7e12;
+constexpr double kStepSecondsPerSubchunk = 1.6e-6;
+constexpr double kBoundarySeconds = 30e-6;
+
+// side_flops: the FLOPs of the products that can move to the side stream,
+// over the whole sequence.
+int time_chunks(const RecGeom& g, int device, double side_flops) {
+  const int knob = g_time_chunks.load();
+  if (knob == 1) return 1;
+  const int sms = sm_count(device);
+  const int free = sms - g.C * g.nclusters;
+  if (g.nclusters > g.max_clusters || free < 1) return 1;
+  if (knob >= 2) return (knob <= kMaxChunks && g.T % (128 * knob) == 0) ? knob : 1;
+  if (g.T % 256 != 0) return 1;
+  const double half = 0.5 * side_flops;
+  const double on_all = half / (sms * kGemmFlopsPerSm);
+  const double on_free = half / (free * kGemmFlopsPerSm);
+  const double loop_half = 0.5 * g.T * (g.bcp / g.R) * kStepSecondsPerSubchunk;
+  const double gain = on_all - std::max(0.0, on_free - loop_half) - kBoundarySeconds;
+  return gain > 0.0 ? 2 : 1;
+}
+
+// One non-blocking side stream per host thread and device (default, i.e.
+// lowest, priority) with a fork and a join event.  Created outside stream
+// capture only: while the caller's stream is capturing and no side stream
+// exists yet, the call runs without time chunks.
+struct Side {
+  cudaStream_t s = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+thread_local std::map<int, Side> t_side;
+
+int side_stream(int device, cudaStream_t main, Side** out) {
+  *out = nullptr;
+  auto it = t_side.find(device);
+  if (it != t_side.end()) {
+    *out = &it->second;
+    return GRU_OK;
+  }
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  GRU_CUDA_TRY(cudaStreamIsCapturing(main, &cs));
+  if (cs != cudaStreamCaptureStatusNone) return GRU_OK;
+  Side sd;
+  GRU_CUDA_TRY(cudaStreamCreateWithFlags(&sd.s, cudaStreamNonBlocking));
+  GRU_CUDA_TRY(cudaEventCreateWithFlags(&sd.fork, cudaEventDisableTiming));
+  GRU_CUDA_TRY(cudaEventCreateWithFlags(&sd.join, cudaEventDisableTiming));
+  *out = &(t_side[device] = sd);
+  return GRU_OK;
+}
+// `to` waits for everything issued so far on `from`.
+int stream_after(cudaStream_t to, cudaStream_t from, cudaEvent_t ev) {
+  GRU_CUDA_TRY(cudaEventRecord(ev, from));
+  GRU_CUDA_TRY(cudaStreamWaitEvent(to, ev, 0));
+  return GRU_OK;
+}
 
 int geometry(int kind, int B, int T, int H, int device, RecGeom* out) {
   {
@@ -134,11 +208,26 @@ BwdLayout bwd_layout(int B, int T, int I, int H, int device) {
   TcGemmArgs ih{nullptr, l.ldgi, nullptr, l.ldx, nullptr, I, nullptr, 3 * H, I, (int)BT, true, true};
   l.gemm = off;
   const TcGemmArgs grads[3] = {hrz, hn, ih};
-  off = align_up(off + tc_gemm_ws_bytes(grads, 3, device), kAlign);
-  // per-cluster FP64 bias-gradient partials written by the backward time loop,
-  // sized for B clusters (an upper bound that needs no device query)
+  // With time chunks the three products are split per chunk (partial slices
+  // of every chunk, summed at the end): room for the largest such plan.  The
+  // split counts grow with the grid, so the full grid bounds them.
+  size_t chunked = 0;
+  for (int n = 2; n <= kMaxChunks; ++n) {
+    if (T % (128 * n) != 0) continue;
+    TcGemmArgs c[3] = {hrz, hn, ih};
+    for (auto& x : c) x.K = (int)(BT / n);
+    int sp[3];
+    tc_partial_splits(c, 3, sm_count(device), sp);
+    size_t bytes = 0;
+    for (int i = 0; i < 3; ++i) bytes += align_up(sizeof(float) * (size_t)n * sp[i] * c[i].M * pad4(c[i].N), kAlign);
+    chunked = std::max(chunked, bytes);
+  }
+  off = align_up(off + std::max(tc_gemm_ws_bytes(grads, 3, device), chunked), kAlign);
+  // per-cluster FP64 bias-gradient partials written by the backward time loop
+  // (one row set per time chunk), sized for B clusters per chunk (an upper
+  // bound that needs no device query)
   l.col = off;
-  off = align_up(off + sizeof(double) * (size_t)B * 4 * H, kAlign);
+  off = align_up(off + sizeof(double) * (size_t)kMaxChunks * B * 4 * H, kAlign);
   l.total = off;
   return l;
 }
@@ -156,6 +245,98 @@ int sm_count(int device) {
   if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) n = 148;
   g_sms[device] = n;
   return n;
+}
+
+// The backward over time chunks (see time_chunks): the loop runs the chunks
+// from the last to the first, the dh state passing between them through
+// dh0; the weight-gradient products (and dx) of every chunk but the first
+// run on the side stream beside the loop over the next earlier chunk, as
+// partial slices that one final launch sums.
+int backward_chunked(const float* dout, const float* dhn, const float* x, const float* w_ih, const float* w_hh,
+                     const float* stash, float* dx, float* dh0, float* dw_ih, float* dw_hh, float* db_ih,
+                     float* db_hh, char* ws, const BwdLayout& l, const RecGeom& g, int nch, const Side& sd, int B,
+                     int T, int I, int H, int dev, cudaStream_t stream) {
+  auto F = [&](size_t off) { return reinterpret_cast<float*>(ws + off); };
+  double* dbpart = reinterpret_cast<double*>(ws + l.col);
+  const int Tc = T / nch, H3 = 3 * H;
+  const int free = sm_count(dev) - g.C * g.nclusters;
+  int rc;
+  const SplitArgs sp[2] = {{stash + 4 * H, (long)B * T, H, 5L * H, F(l.hph), F(l.hpl), l.ldh},
+                           {x, (long)B * T, I, I, F(l.xh), F(l.xl), l.ldx}};
+  // Products of chunk c (rows b*T + t for t in [c*Tc, c*Tc + Tc)).
+  TcGemmArgs full[3] = {
+      {F(l.dgih), l.ldgi, F(l.hph), l.ldh, dw_hh, H, nullptr, 2 * H, H, B * T, true, true, F(l.dgil), F(l.hpl)},
+      {F(l.dghh), l.ldh, F(l.hph), l.ldh, dw_hh + 2L * H * H, H, nullptr, H, H, B * T, true, true, F(l.dghl),
+       F(l.hpl)},
+      {F(l.dgih), l.ldgi, F(l.xh), l.ldx, dw_ih, I, nullptr, H3, I, B * T, true, true, F(l.dgil), F(l.xl)}};
+  float* part[3];
+  long ldp[3];
+  int zoff[3] = {0, 0, 0};
+  {
+    char* p = ws + l.gemm;
+    int spmax[3];
+    TcGemmArgs c[3] = {full[0], full[1], full[2]};
+    for (auto& a : c) a.K = B * Tc;
+    tc_partial_splits(c, 3, sm_count(dev), spmax);
+    for (int i = 0; i < 3; ++i) {
+      part[i] = reinterpret_cast<float*>(p);
+      ldp[i] = pad4(full[i].N);
+      p += align_up(sizeof(float) * (size_t)nch * spmax[i] * full[i].M * ldp[i], kAlign);
+    }
+  }
+  auto products = [&](int c, cudaStream_t s, int ctas) -> int {
+    const size_t t0 = (size_t)c * Tc;
+    TcGemmArgs a[3] = {full[0], full[1], full[2]};
+    for (auto& q : a) {
+      q.K = B * Tc;
+      q.rin = Tc;
+      q.rstride = T;
+    }
+    a[0].A = F(l.dgih) + t0 * l.ldgi, a[0].A_lo = F(l.dgil) + t0 * l.ldgi;
+    a[0].B = F(l.hph) + t0 * l.ldh, a[0].B_lo = F(l.hpl) + t0 * l.ldh;
+    a[1].A = F(l.dghh) + t0 * l.ldh, a[1].A_lo = F(l.dghl) + t0 * l.ldh;
+    a[1].B = a[0].B, a[1].B_lo = a[0].B_lo;
+    a[2].A = a[0].A, a[2].A_lo = a[0].A_lo;
+    a[2].B = F(l.xh) + t0 * l.ldx, a[2].B_lo = F(l.xl) + t0 * l.ldx;
+    if (int r = tc_gemm_partials(a, 3, s, kKindGradGemm, ctas, part, ldp, zoff)) return r;
+    if (dx) {
+      // dx rows of chunk c = dG_ih rows . W_ih, with W_ih^T staged as [I, ldgi]
+      TcGemmArgs d{F(l.dgih) + t0 * l.ldgi, l.ldgi, F(l.wth), l.ldgi, dx + t0 * I, I, nullptr, B * Tc, I, H3,
+                   false, false, F(l.dgil) + t0 * l.ldgi, F(l.wtl)};
+      d.rin = Tc;
+      d.rstride = T;
+      if (int r = tc_gemm(d, s, kKindGradGemm, nullptr, 0, ctas)) return r;
+    }
+    return GRU_OK;
+  };
+  // Every loop is issued before the side work that runs beside it, so that
+  // the loop's clusters are placed first; the side stream waits on the fork
+  // event as recorded before that loop was issued.
+  GRU_CUDA_TRY(cudaEventRecord(sd.fork, stream));
+  for (int c = nch - 1; c >= 0; --c) {
+    if ((rc = launch_rec_backward(dout, c == nch - 1 ? dhn : dh0, w_hh, stash, F(l.dgih), F(l.dgil), l.ldgi,
+                                  F(l.dghh), F(l.dghl), l.ldh, dh0, dbpart + (size_t)(nch - 1 - c) * g.nclusters * 4 * H,
+                                  g, stream, c * Tc, Tc)))
+      return rc;
+    GRU_CUDA_TRY(cudaStreamWaitEvent(sd.s, sd.fork, 0));
+    if (c == nch - 1) {
+      // the split copies of h_prev and x (and W_ih^T for dx) beside the first loop
+      if ((rc = split_tf32_multi(sp, 2, sd.s))) return rc;
+      if (dx) {
+        if ((rc = transpose(w_ih, H3, I, F(l.wt), l.ldgi, sd.s))) return rc;
+        if ((rc = split_tf32(F(l.wt), I, l.ldgi, l.ldgi, F(l.wth), F(l.wtl), l.ldgi, sd.s))) return rc;
+      }
+    } else {
+      // chunk c+1's products beside the loop over chunk c
+      if ((rc = products(c + 1, sd.s, free))) return rc;
+    }
+    GRU_CUDA_TRY(cudaEventRecord(sd.fork, stream));
+  }
+  if ((rc = stream_after(stream, sd.s, sd.join))) return rc;
+  if ((rc = products(0, stream, 0))) return rc;
+  int ns[3] = {zoff[0], zoff[1], zoff[2]};
+  if ((rc = tc_gemm_sum(full, 3, part, ldp, ns, stream, kKindGradGemm))) return rc;
+  return bias_grads_finish(dbpart, nch * g.nclusters, H, db_ih, db_hh, stream);
 }
 
 }  // namespace gru
@@ -178,6 +359,11 @@ int gru_device_supported(int device) {
     return 0;
   }
   return major == 10 ? 1 : 0;
+}
+
+int gru_set_time_chunks(int n) {
+  if (n < 0 || n > kMaxChunks) return -1;
+  return g_time_chunks.exchange(n);
 }
 
 int gru_device_status(int reset) {
@@ -221,6 +407,17 @@ int gru_forward(const float* x, const float* h0, const float* w_ih, const float*
                 const float* b_ih, const float* b_hh, float* out, float* hn, float* stash,
                 void* workspace, size_t workspace_bytes, int B, int T, int I, int H,
                 void* stream_) {
+  return gru::forward_impl(x, h0, w_ih, w_hh, b_ih, b_hh, out, hn, stash, workspace, workspace_bytes, B, T, I, H,
+                           stream_, true);
+}
+
+}  // extern "C"
+
+namespace gru {
+
+int forward_impl(const float* x, const float* h0, const float* w_ih, const float* w_hh, const float* b_ih,
+                 const float* b_hh, float* out, float* hn, float* stash, void* workspace, size_t workspace_bytes,
+                 int B, int T, int I, int H, void* stream_, bool overlap) {
   clear_error();
   int rc = check_shape(B, T, I, H);
   if (rc) return rc;
@@ -251,11 +448,49 @@ int gru_forward(const float* x, const float* h0, const float* w_ih, const float*
   const SplitArgs sp[2] = {{x, (long)B * T, I, I, xh, xl, l.ldx}, {w_ih, 3L * H, I, I, wh, wl, l.ldx}};
   if ((rc = split_tf32_multi(sp, 2, stream))) return rc;
   TcGemmArgs ga{xh, l.ldx, wh, l.ldx, G, l.ldg, b_ih, B * T, 3 * H, I, false, false, xl, wl};
-  if ((rc = tc_gemm(ga, stream, kKindInputGemm))) return rc;
   RecGeom g{};
   if ((rc = geometry(0, B, T, H, dev, &g))) return rc;
-  return launch_rec_forward(G, l.ldg, h0, w_hh, b_hh, out, hn, stash, g, stream);
+  const int nch = overlap ? time_chunks(g, dev, 2.0 * B * T * 3.0 * H * I) : 1;
+  Side* sd = nullptr;
+  if (nch > 1 && (rc = side_stream(dev, stream, &sd))) return rc;
+  if (nch == 1 || sd == nullptr) {
+    if ((rc = tc_gemm(ga, stream, kKindInputGemm))) return rc;
+    return launch_rec_forward(G, l.ldg, h0, w_hh, b_hh, out, hn, stash, g, stream);
+  }
+  // Time chunks: the projection of chunk 0 on the whole GPU, then the loop
+  // over chunk c beside the projection of chunk c+1 (side stream, on the SMs
+  // the loop leaves idle).  The state passes between chunks through hn.
+  const int Tc = T / nch;
+  const int free = sm_count(dev) - g.C * g.nclusters;
+  auto chunk = [&](int c) {
+    TcGemmArgs a = ga;
+    a.A = xh + (size_t)c * Tc * l.ldx;
+    a.A_lo = xl + (size_t)c * Tc * l.ldx;
+    a.C = G + (size_t)c * Tc * l.ldg;
+    a.M = B * Tc;
+    a.rin = Tc;
+    a.rstride = T;
+    return a;
+  };
+  // Every loop is issued before the product that runs beside it, so that
+  // the loop's clusters are placed first.
+  if ((rc = tc_gemm(chunk(0), stream, kKindInputGemm))) return rc;
+  GRU_CUDA_TRY(cudaEventRecord(sd->fork, stream));
+  for (int c = 0; c < nch; ++c) {
+    if ((rc = launch_rec_forward(G, l.ldg, c == 0 ? h0 : hn, w_hh, b_hh, out, hn, stash, g, stream, c * Tc, Tc)))
+      return rc;
+    if (c + 1 < nch) {
+      if (c == 0) GRU_CUDA_TRY(cudaStreamWaitEvent(sd->s, sd->fork, 0));
+      if ((rc = tc_gemm(chunk(c + 1), sd->s, kKindInputGemm, nullptr, 0, free))) return rc;
+      if ((rc = stream_after(stream, sd->s, sd->join))) return rc;  // the loop over chunk c+1 needs it
+    }
+  }
+  return GRU_OK;
 }
+
+}  // namespace gru
+
+extern "C" {
 
 int gru_backward(const float* dout, const float* dhn, const float* x, const float* w_ih,
                  const float* w_hh, const float* stash, float* dx, float* dh0, float* dw_ih,
@@ -298,12 +533,18 @@ int gru_backward(const float* dout, const float* dhn, const float* x, const floa
   void* gws = ws + l.gemm;
   const size_t gws_bytes = l.col - l.gemm;
   double* dbpart = reinterpret_cast<double*>(ws + l.col);
+  const int BT = B * T;
+  const int H3 = 3 * H;
+  const int nch = time_chunks(g, dev, 2.0 * B * T * 3.0 * H * (H + I + (dx ? I : 0)));
+  Side* sd = nullptr;
+  if (nch > 1 && (rc = side_stream(dev, stream, &sd))) return rc;
+  if (nch > 1 && sd != nullptr)
+    return backward_chunked(dout, dhn, x, w_ih, w_hh, stash, dx, dh0, dw_ih, dw_hh, db_ih, db_hh, ws, l, g, nch, *sd,
+                            B, T, I, H, dev, stream);
   if ((rc = launch_rec_backward(dout, dhn, w_hh, stash, F(l.dgih), F(l.dgil), l.ldgi, F(l.dghh), F(l.dghl), l.ldh,
                                 dh0, dbpart, g, stream)))
     return rc;
 
-  const int BT = B * T;
-  const int H3 = 3 * H;
   // dW_hh = dG_hh^T . h_prev (h_prev = stash column block 4), dW_ih = dG_ih^T . x
   // on the tensor cores from pre-split copies.  dW_hh's r/z rows come from
   // dG_ih's r/z columns, its n rows from the separate n block.

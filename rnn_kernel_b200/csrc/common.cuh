@@ -58,16 +58,19 @@ int wait_probe(unsigned long long limit_ns, int* result_dev, cudaStream_t stream
 int rec_forward_geometry(int B, int T, int H, int device, RecGeom* g);
 int rec_backward_geometry(int B, int T, int H, int device, RecGeom* g);
 
-// G: input gates [B*T rows, 3H], row stride ldg floats.
+// G: input gates [B*T rows, 3H], row stride ldg floats.  Both time loops
+// run the steps [t0, t0 + nt) (nt < 0: the whole sequence); the state enters
+// through h0 / dhn and leaves through hn / dh0, so a sequence can be run as
+// consecutive time chunks.
 int launch_rec_forward(const float* G, int ldg, const float* h0, const float* w_hh, const float* b_hh,
                        float* out, float* hn, float* stash, const RecGeom& g,
-                       cudaStream_t stream);
+                       cudaStream_t stream, int t0 = 0, int nt = -1);
 // dG_ih [rows, 3H] (row stride ldgi) and the n block of dG_hh [rows, H] (row
 // stride ldgn) are written pre-split (hi, lo).
 int launch_rec_backward(const float* dout, const float* dhn, const float* w_hh,
                         const float* stash, float* dGi, float* dGi_lo, int ldgi, float* dGh, float* dGh_lo,
                         int ldgn, float* dh0, double* dbpart,
-                        const RecGeom& g, cudaStream_t stream);
+                        const RecGeom& g, cudaStream_t stream, int t0 = 0, int nt = -1);
 
 // Tensor-core (tcgen05, 3xTF32) product C[m, n] = sum_k A(m, k) B(n, k) (+ bias).
 // The operands come pre-split: A / A_lo hold tf32(a) and tf32(a - tf32(a))
@@ -87,6 +90,14 @@ struct TcGemmArgs {
   bool a_mn = false, b_mn = false;
   const float* A_lo = nullptr;
   const float* B_lo = nullptr;
+  // Periodic rows: the operands whose rows are the B*T (batch, step) rows --
+  // A (its M rows when K-major, its K rows when MN-major), B when MN-major,
+  // and C when A is K-major -- hold logical row r at physical row
+  // (r / rin) * rstride + r % rin: with the pointers offset by t0 rows,
+  // rin = steps of a time chunk and rstride = T select that chunk's rows of
+  // every batch row.  rin = 0: plain rows.
+  int rin = 0;
+  long rstride = 0;
 };
 // hi[r, c] = tf32(src[r, c]), lo[r, c] = tf32(src - hi) for c < cols, 0 for
 // cols <= c < ldd; src row stride lds, outputs row stride ldd.
@@ -104,12 +115,28 @@ struct SplitArgs {
 int split_tf32_multi(const SplitArgs* a, int n, cudaStream_t stream);
 bool tc_gemm_supported(const TcGemmArgs& a);
 size_t tc_gemm_ws_bytes(const TcGemmArgs& a, int device);
-int tc_gemm(const TcGemmArgs& a, cudaStream_t stream, int kind, void* ws = nullptr, size_t ws_bytes = 0);
+// ctas > 0 caps the persistent grid (the rest of the SMs stay free for work
+// running concurrently on another stream).
+int tc_gemm(const TcGemmArgs& a, cudaStream_t stream, int kind, void* ws = nullptr, size_t ws_bytes = 0,
+            int ctas = 0);
 // 1 to 3 products with the same operand majors in ONE launch (a persistent
 // grid over all of their tiles and K splits) plus one launch summing all
 // split-K partials; the workspace holds every product's partials.
 size_t tc_gemm_ws_bytes(const TcGemmArgs* a, int n, int device);
-int tc_gemm_batch(const TcGemmArgs* a, int n, cudaStream_t stream, int kind, void* ws, size_t ws_bytes);
+int tc_gemm_batch(const TcGemmArgs* a, int n, cudaStream_t stream, int kind, void* ws, size_t ws_bytes,
+                  int ctas = 0);
+// Partial products without the final sum, for products summed over several
+// launches (e.g. one per time chunk): problem i is split over K into
+// splits[i] pieces (tc_partial_splits, for a grid of `ctas` CTAs) written as
+// slices zoff[i], zoff[i] + 1, ... of part[i] ([slice][M][ldp[i]] floats);
+// zoff[i] advances by the slices written.  tc_gemm_sum then writes
+// C = sum of the first nslices[i] slices (FP64, fixed order).
+int tc_partial_splits(const TcGemmArgs* a, int n, int ctas, int* splits);
+int tc_gemm_partials(const TcGemmArgs* a, int n, cudaStream_t stream, int kind, int ctas, float* const* part,
+                     const long* ldp, int* zoff);
+int tc_gemm_sum(const TcGemmArgs* a, int n, const float* const* part, const long* ldp, const int* nslices,
+                cudaStream_t stream, int kind);
+bool tc_rows_ok(const TcGemmArgs& a);
 int read_gemm_status(int reset, int* status);
 
 // Transpose a [rows, cols] matrix into [cols, ldd] (columns rows .. ldd zeroed).
@@ -122,6 +149,12 @@ int transpose(const float* src, int rows, int cols, float* dst, int ldd, cudaStr
 int bias_grads_finish(const double* part, int nparts, int H, float* db_ih, float* db_hh, cudaStream_t stream);
 
 int sm_count(int device);
+
+// gru_forward's body; overlap = false keeps the whole forward on `stream`
+// (no time chunks, no side stream), as the allocation-free entry point needs.
+int forward_impl(const float* x, const float* h0, const float* w_ih, const float* w_hh, const float* b_ih,
+                 const float* b_hh, float* out, float* hn, float* stash, void* workspace, size_t workspace_bytes,
+                 int B, int T, int I, int H, void* stream, bool overlap);
 
 // ---------------------------------------------------------------------------
 // Launch accounting and optional per-kernel CUDA-event timing (host side).

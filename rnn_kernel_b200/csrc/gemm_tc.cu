@@ -26,6 +26,7 @@
 
 #include <cuda.h>
 
+#include <algorithm>
 #include <cstring>
 
 #include "common.cuh"
@@ -84,10 +85,17 @@ __device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
   }
 }
 
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+// Every operand map is 3-D: (column, row within a period, period).  A plain
+// matrix has one period; the rows of a time chunk of a [B*T, cols] matrix
+// (rows b*T + t for t in a window of rin steps) have B periods of rin rows.
+// Logical row r is (r % rin, r / rin); a box never straddles a period (rin is
+// a multiple of the box's rows whenever there is more than one period).
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int r,
+                                            int rin) {
+  const int y = r % rin, z = r / rin;
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
 
@@ -181,6 +189,9 @@ struct Smem {
 constexpr int kMaxProblems = 3;
 struct GemmProblem {
   CUtensorMap ah, al, bh, bl;  // A hi/lo, B hi/lo tensor maps
+  int a_rin, b_rin;             // rows per period of the A / B maps
+  int c_rin;                    // C rows: logical row r is stored at row (r / c_rin) * c_rstride + r % c_rin
+  long c_rstride;
   float* C;
   long ldc;
   const float* bias;
@@ -294,25 +305,26 @@ gemm_tf32x3_kernel(const __grid_constant__ GemmBatch bt) {
           const CUtensorMap* map_al = &bt.p[w.pi].al;
           const CUtensorMap* map_bh = &bt.p[w.pi].bh;
           const CUtensorMap* map_bl = &bt.p[w.pi].bl;
+          const int arin = bt.p[w.pi].a_rin, brin = bt.p[w.pi].b_rin;
           if (A_MN) {
 #pragma unroll
             for (int j = 0; j < kBM / 32; ++j) {
-              tma_load_2d(a_hi + j * 4096, map_ah, full(s), w.m0 + 32 * j, k0);
-              tma_load_2d(a_lo + j * 4096, map_al, full(s), w.m0 + 32 * j, k0);
+              tma_load_3d(a_hi + j * 4096, map_ah, full(s), w.m0 + 32 * j, k0, arin);
+              tma_load_3d(a_lo + j * 4096, map_al, full(s), w.m0 + 32 * j, k0, arin);
             }
           } else {
-            tma_load_2d(a_hi, map_ah, full(s), k0, w.m0);
-            tma_load_2d(a_lo, map_al, full(s), k0, w.m0);
+            tma_load_3d(a_hi, map_ah, full(s), k0, w.m0, arin);
+            tma_load_3d(a_lo, map_al, full(s), k0, w.m0, arin);
           }
           if (B_MN) {
 #pragma unroll
             for (int j = 0; j < BN / 32; ++j) {
-              tma_load_2d(b_hi + j * 4096, map_bh, full(s), w.n0 + 32 * j, k0);
-              tma_load_2d(b_lo + j * 4096, map_bl, full(s), w.n0 + 32 * j, k0);
+              tma_load_3d(b_hi + j * 4096, map_bh, full(s), w.n0 + 32 * j, k0, brin);
+              tma_load_3d(b_lo + j * 4096, map_bl, full(s), w.n0 + 32 * j, k0, brin);
             }
           } else {
-            tma_load_2d(b_hi, map_bh, full(s), k0, w.n0);
-            tma_load_2d(b_lo, map_bl, full(s), k0, w.n0);
+            tma_load_3d(b_hi, map_bh, full(s), k0, w.n0, brin);
+            tma_load_3d(b_lo, map_bl, full(s), k0, w.n0, brin);
           }
         }
       }
@@ -395,6 +407,9 @@ gemm_tf32x3_kernel(const __grid_constant__ GemmBatch bt) {
       const GemmProblem& P = bt.p[w.pi];
       const int M = P.M, N = P.N;
       const long ldc = P.ldc;
+      const int crin = P.c_rin;
+      const long crs = P.c_rstride;
+      auto crow_of = [&](int r) -> long { return crin > 0 ? (long)(r / crin) * crs + r % crin : (long)r; };
       const int row = w.m0 + 32 * quarter + lane;
       const int n0 = w.n0 + kCW * chalf;
       float* Cu = P.splits > 1 ? P.C + (long)w.split * M * ldc : P.C;
@@ -432,13 +447,13 @@ gemm_tf32x3_kernel(const __grid_constant__ GemmBatch bt) {
             const int r = i * 8 + (lane >> 2), q = lane & 3;
             if (rbase + r < M) {
               const float4 e = *reinterpret_cast<const float4*>(eb + r * L::kEpiPitch + 4 * (q ^ ((r >> 1) & 3)));
-              *reinterpret_cast<float4*>(Cu + (long)(rbase + r) * ldc + n0 + c0 + 4 * q) = e;
+              *reinterpret_cast<float4*>(Cu + crow_of(rbase + r) * ldc + n0 + c0 + 4 * q) = e;
             }
           }
           __syncwarp();
         }
       } else if (row < M) {
-        float* crow = Cu + (long)row * ldc + n0;
+        float* crow = Cu + crow_of(row) * ldc + n0;
         {
 #pragma unroll
           for (int c = 0; c < kCW; ++c) {
@@ -482,18 +497,22 @@ int encode_fn(EncodeTiledFn* out) {
   return GRU_OK;
 }
 
-// 2-D fp32 tensor map over a row-major [rows, cols] matrix (row stride ld
-// floats), box = box_cols (inner) x box_rows, 128-byte swizzle.
+// 3-D fp32 tensor map over the logical rows of a row-major matrix (row stride
+// ld floats): `periods` blocks of `rin` consecutive rows, block p starting
+// at row p * rstride (one block of rows rows for a plain matrix);
+// box = box_cols (inner) x box_rows x 1, 128-byte swizzle.
 int make_map(CUtensorMap* map, const float* ptr, long rows, long cols, long ld, int box_cols, int box_rows,
-             bool mn_major) {
+             bool mn_major, int rin = 0, long rstride = 0) {
   EncodeTiledFn enc = nullptr;
   int rc = encode_fn(&enc);
   if (rc) return rc;
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
-  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box, estr,
+  const long in = rin > 0 ? rin : rows;
+  const long periods = rin > 0 ? rows / rin : 1;
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)in, (cuuint64_t)periods};
+  cuuint64_t strides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)(rin > 0 ? rstride : rows) * ld * 4};
+  cuuint32_t box[3] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(ptr), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE,
                    mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -534,13 +553,14 @@ __global__ void splitk_sum_kernel(const __grid_constant__ SplitSumBatch sb) {
 }
 
 constexpr int kBN = 128, kS = 3, kNPAIR = 2;
+constexpr int kMaxStagesPerSplit = 128;  // K stages (32 rows each) summed in FP32 by one split
 using LDefault = Smem<kBN, kS>;
 
 // One launch for problems a[0..n) (same operand majors); problem i writes
 // to C[i] (row stride ldc[i]) with splits[i] K splits of kchunk[i].
 template <bool A_MN, bool B_MN>
 int launch_tc(const TcGemmArgs* a, int n, float* const* C, const long* ldc, const int* splits, const int* kchunk,
-              cudaStream_t stream) {
+              cudaStream_t stream, int ctas) {
   auto kern = gemm_tf32x3_kernel<kBN, kS, kNPAIR, A_MN, B_MN>;
   static thread_local int configured_device = -1;
   int dev = 0;
@@ -556,19 +576,30 @@ int launch_tc(const TcGemmArgs* a, int n, float* const* C, const long* ldc, cons
   for (int i = 0; i < n; ++i) {
     GemmProblem& P = bt.p[i];
     int rc;
+    // rin / rstride describe the rows of the [B*T]-row operands: A's rows (M
+    // when K-major, K when MN-major), B's K rows when MN-major, and C's rows
+    // when A is K-major (the input projection).
+    const int rin = a[i].rin;
+    const long rs = a[i].rstride;
     if (A_MN) {
-      if ((rc = make_map(&P.ah, a[i].A, a[i].K, a[i].M, a[i].lda, 32, kBK, true))) return rc;
-      if ((rc = make_map(&P.al, a[i].A_lo, a[i].K, a[i].M, a[i].lda, 32, kBK, true))) return rc;
+      if ((rc = make_map(&P.ah, a[i].A, a[i].K, a[i].M, a[i].lda, 32, kBK, true, rin, rs))) return rc;
+      if ((rc = make_map(&P.al, a[i].A_lo, a[i].K, a[i].M, a[i].lda, 32, kBK, true, rin, rs))) return rc;
+      P.a_rin = rin > 0 ? rin : a[i].K;
     } else {
-      if ((rc = make_map(&P.ah, a[i].A, a[i].M, a[i].K, a[i].lda, kBK, kBM, false))) return rc;
-      if ((rc = make_map(&P.al, a[i].A_lo, a[i].M, a[i].K, a[i].lda, kBK, kBM, false))) return rc;
+      if ((rc = make_map(&P.ah, a[i].A, a[i].M, a[i].K, a[i].lda, kBK, kBM, false, rin, rs))) return rc;
+      if ((rc = make_map(&P.al, a[i].A_lo, a[i].M, a[i].K, a[i].lda, kBK, kBM, false, rin, rs))) return rc;
+      P.a_rin = rin > 0 ? rin : a[i].M;
+      P.c_rin = rin;
+      P.c_rstride = rs;
     }
     if (B_MN) {
-      if ((rc = make_map(&P.bh, a[i].B, a[i].K, a[i].N, a[i].ldb, 32, kBK, true))) return rc;
-      if ((rc = make_map(&P.bl, a[i].B_lo, a[i].K, a[i].N, a[i].ldb, 32, kBK, true))) return rc;
+      if ((rc = make_map(&P.bh, a[i].B, a[i].K, a[i].N, a[i].ldb, 32, kBK, true, rin, rs))) return rc;
+      if ((rc = make_map(&P.bl, a[i].B_lo, a[i].K, a[i].N, a[i].ldb, 32, kBK, true, rin, rs))) return rc;
+      P.b_rin = rin > 0 ? rin : a[i].K;
     } else {
       if ((rc = make_map(&P.bh, a[i].B, a[i].N, a[i].K, a[i].ldb, kBK, kBN, false))) return rc;
       if ((rc = make_map(&P.bl, a[i].B_lo, a[i].N, a[i].K, a[i].ldb, kBK, kBN, false))) return rc;
+      P.b_rin = a[i].N;
     }
     P.C = C[i];
     P.ldc = ldc[i];
@@ -584,7 +615,8 @@ int launch_tc(const TcGemmArgs* a, int n, float* const* C, const long* ldc, cons
     P.unit_end = units;
   }
   bt.units = units;
-  const int grid = units < sm_count(dev) ? units : sm_count(dev);
+  const int cap = ctas > 0 && ctas < sm_count(dev) ? ctas : sm_count(dev);
+  const int grid = units < cap ? units : cap;
   kern<<<grid, kThreads, LDefault::kBytes, stream>>>(bt);
   GRU_CUDA_TRY(cudaGetLastError());
   return GRU_OK;
@@ -693,6 +725,21 @@ int read_gemm_status(int reset, int* status) {
   return GRU_OK;
 }
 
+// Periodic rows (a time chunk of [B*T]-row operands): the logical row count
+// of every periodic operand (M for a K-major A, K for MN-major ones) must be
+// whole periods, and a TMA box must not straddle two periods.
+bool tc_rows_ok(const TcGemmArgs& a) {
+  if (a.rin <= 0) return true;
+  const bool ok_m = a.a_mn || (a.rin % kBM == 0 && a.M % a.rin == 0);
+  const bool ok_k = !(a.a_mn || a.b_mn) || (a.rin % kBK == 0 && a.K % a.rin == 0);
+  const bool ok_s = a.rstride >= a.rin && a.rstride % 4 == 0;
+  if (!(ok_m && ok_k && ok_s)) {
+    set_error("tc_gemm: periodic rows need whole periods of a multiple of the tile rows");
+    return false;
+  }
+  return true;
+}
+
 bool tc_gemm_supported(const TcGemmArgs& a) {
   if (!a.A_lo || !a.B_lo) return false;
   return ((reinterpret_cast<uintptr_t>(a.A_lo) | reinterpret_cast<uintptr_t>(a.B_lo)) & 15) == 0 && ((reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.B)) & 15) == 0 &&
@@ -702,8 +749,9 @@ bool tc_gemm_supported(const TcGemmArgs& a) {
 // K splits of the products of one launch: long K (the weight gradients,
 // K = B*T) with few output tiles is split so that the whole batch covers the
 // SMs about twice, each problem's share in proportion to its work, keeping
-// >= 8 K stages per split.  Without a workspace nothing is split.
-void tc_splits(const TcGemmArgs* a, int n, int device, int* out) {
+// >= 8 and (where that allows) <= kMaxStagesPerSplit K stages per split.
+// Without a workspace nothing is split.
+void tc_splits_ctas(const TcGemmArgs* a, int n, int ctas, int* out) {
   long work = 0;
   for (int i = 0; i < n; ++i)
     work += (long)((a[i].M + kBM - 1) / kBM) * ((a[i].N + kBN - 1) / kBN) * ((a[i].K + kBK - 1) / kBK);
@@ -711,11 +759,17 @@ void tc_splits(const TcGemmArgs* a, int n, int device, int* out) {
     const int tiles = ((a[i].M + kBM - 1) / kBM) * ((a[i].N + kBN - 1) / kBN);
     const int stages = (a[i].K + kBK - 1) / kBK;
     const double share = work > 0 ? (double)tiles * stages / (double)work : 1.0;
-    int s = (int)(2.0 * sm_count(device) * share / tiles + 0.5);
+    int s = (int)(2.0 * ctas * share / tiles + 0.5);
+    // Accuracy: each split's FP32 register sum covers at most
+    // kMaxStagesPerSplit stages (long FP32 sums lose digits; the FP64
+    // reduce of the splits does not).
+    s = std::max(s, (stages + kMaxStagesPerSplit - 1) / kMaxStagesPerSplit);
     if (s > stages / 8) s = stages / 8;
     out[i] = s < 1 ? 1 : s;
   }
 }
+
+void tc_splits(const TcGemmArgs* a, int n, int device, int* out) { tc_splits_ctas(a, n, sm_count(device), out); }
 
 size_t tc_gemm_ws_bytes(const TcGemmArgs* a, int n, int device) {
   int sp[kMaxProblems];
@@ -729,7 +783,7 @@ size_t tc_gemm_ws_bytes(const TcGemmArgs* a, int n, int device) {
 
 size_t tc_gemm_ws_bytes(const TcGemmArgs& a, int device) { return tc_gemm_ws_bytes(&a, 1, device); }
 
-int tc_gemm_batch(const TcGemmArgs* a, int n, cudaStream_t stream, int kind, void* ws, size_t ws_bytes) {
+int tc_gemm_batch(const TcGemmArgs* a, int n, cudaStream_t stream, int kind, void* ws, size_t ws_bytes, int ctas) {
   if (n < 1 || n > kMaxProblems) {
     set_error("tc_gemm: 1 to 3 products per launch");
     return GRU_ERR_INVALID;
@@ -767,6 +821,7 @@ int tc_gemm_batch(const TcGemmArgs* a, int n, cudaStream_t stream, int kind, voi
       set_error("tc_gemm: the products of one launch must share their operand majors");
       return GRU_ERR_INVALID;
     }
+    if (!tc_rows_ok(a[i])) return GRU_ERR_INVALID;
     kc[i] = sp[i] > 1 ? ((a[i].K + sp[i] * kBK - 1) / (sp[i] * kBK)) * kBK : a[i].K;
     C[i] = a[i].C;
     ldc[i] = a[i].ldc;
@@ -799,8 +854,8 @@ int tc_gemm_batch(const TcGemmArgs* a, int n, cudaStream_t stream, int kind, voi
   if (live == 0) return GRU_OK;
   LaunchScope scope(kind, stream, sb.nq > 0 ? 2 : 1);
   int rc;
-  if (run[0].a_mn && run[0].b_mn) rc = launch_tc<true, true>(run, live, rC, rldc, rsp, rkc, stream);
-  else if (!run[0].a_mn && !run[0].b_mn) rc = launch_tc<false, false>(run, live, rC, rldc, rsp, rkc, stream);
+  if (run[0].a_mn && run[0].b_mn) rc = launch_tc<true, true>(run, live, rC, rldc, rsp, rkc, stream, ctas);
+  else if (!run[0].a_mn && !run[0].b_mn) rc = launch_tc<false, false>(run, live, rC, rldc, rsp, rkc, stream, ctas);
   else {
     set_error("tc_gemm: mixed operand majors are not instantiated");
     return GRU_ERR_INVALID;
@@ -813,8 +868,76 @@ int tc_gemm_batch(const TcGemmArgs* a, int n, cudaStream_t stream, int kind, voi
   return GRU_OK;
 }
 
-int tc_gemm(const TcGemmArgs& a, cudaStream_t stream, int kind, void* ws, size_t ws_bytes) {
-  return tc_gemm_batch(&a, 1, stream, kind, ws, ws_bytes);
+int tc_gemm(const TcGemmArgs& a, cudaStream_t stream, int kind, void* ws, size_t ws_bytes, int ctas) {
+  return tc_gemm_batch(&a, 1, stream, kind, ws, ws_bytes, ctas);
+}
+
+int tc_partial_splits(const TcGemmArgs* a, int n, int ctas, int* splits) {
+  if (n < 1 || n > kMaxProblems) {
+    set_error("tc_gemm: 1 to 3 products per launch");
+    return GRU_ERR_INVALID;
+  }
+  tc_splits_ctas(a, n, ctas, splits);
+  return GRU_OK;
+}
+
+int tc_gemm_partials(const TcGemmArgs* a, int n, cudaStream_t stream, int kind, int ctas, float* const* part,
+                     const long* ldp, int* zoff) {
+  int dev = 0;
+  GRU_CUDA_TRY(cudaGetDevice(&dev));
+  if (ctas <= 0 || ctas > sm_count(dev)) ctas = sm_count(dev);
+  int sp[kMaxProblems], kc[kMaxProblems];
+  if (int rc = tc_partial_splits(a, n, ctas, sp)) return rc;
+  float* C[kMaxProblems];
+  long ldc[kMaxProblems];
+  for (int i = 0; i < n; ++i) {
+    if (a[i].M <= 0 || a[i].N <= 0 || a[i].K <= 0 || !tc_gemm_supported(a[i]) || a[i].bias ||
+        a[i].a_mn != a[0].a_mn || a[i].b_mn != a[0].b_mn || ldp[i] % 4 != 0 || ldp[i] < a[i].N) {
+      set_error("tc_gemm_partials: unsupported product");
+      return GRU_ERR_INVALID;
+    }
+    if (!tc_rows_ok(a[i])) return GRU_ERR_INVALID;
+    kc[i] = ((a[i].K + sp[i] * kBK - 1) / (sp[i] * kBK)) * kBK;
+    C[i] = part[i] + (long)zoff[i] * a[i].M * ldp[i];
+    ldc[i] = ldp[i];
+    zoff[i] += sp[i];
+  }
+  LaunchScope scope(kind, stream);
+  if (a[0].a_mn && a[0].b_mn) return launch_tc<true, true>(a, n, C, ldc, sp, kc, stream, ctas);
+  if (!a[0].a_mn && !a[0].b_mn) return launch_tc<false, false>(a, n, C, ldc, sp, kc, stream, ctas);
+  set_error("tc_gemm: mixed operand majors are not instantiated");
+  return GRU_ERR_INVALID;
+}
+
+int tc_gemm_sum(const TcGemmArgs* a, int n, const float* const* part, const long* ldp, const int* nslices,
+                cudaStream_t stream, int kind) {
+  if (n < 1 || n > kMaxProblems) {
+    set_error("tc_gemm_sum: 1 to 3 products");
+    return GRU_ERR_INVALID;
+  }
+  SplitSumBatch sb;
+  memset(&sb, 0, sizeof(sb));
+  long elems = 0;
+  for (int i = 0; i < n; ++i) {
+    if (a[i].M <= 0 || a[i].N <= 0) continue;
+    SplitSum& Q = sb.q[sb.nq++];
+    Q.part = part[i];
+    Q.C = a[i].C;
+    Q.ldp = ldp[i];
+    Q.ldc = a[i].ldc;
+    Q.S = nslices[i];
+    Q.M = a[i].M;
+    Q.N = a[i].N;
+    elems += (long)a[i].M * a[i].N;
+    Q.end = elems;
+  }
+  if (sb.nq == 0) return GRU_OK;
+  int dev = 0;
+  GRU_CUDA_TRY(cudaGetDevice(&dev));
+  LaunchScope scope(kind, stream);
+  splitk_sum_kernel<<<sm_count(dev) * 4, 256, 0, stream>>>(sb);
+  GRU_CUDA_TRY(cudaGetLastError());
+  return GRU_OK;
 }
 
 }  // namespace gru

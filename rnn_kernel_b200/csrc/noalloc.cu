@@ -83,6 +83,6 @@ extern "C" int gru_forward_inference_noalloc(const float* x, const float* h0, co
   void* scratch = nullptr;
   int rc = scratch_address(dev, &scratch);
   if (rc) return rc;
-  return gru_forward(x, h0, w_ih, w_hh, b_ih, b_hh, out, hn, nullptr, scratch,
-                     (size_t)GRU_NOALLOC_SCRATCH_BYTES, B, T, I, H, stream);
+  return forward_impl(x, h0, w_ih, w_hh, b_ih, b_hh, out, hn, nullptr, scratch,
+                      (size_t)GRU_NOALLOC_SCRATCH_BYTES, B, T, I, H, stream, false);
 }

@@ -167,6 +167,10 @@ struct FwdArgs {
   float* out;         // [B,T,H]
   float* hn;          // [B,H]
   float* stash;       // [B,T,5H] or null
+  // Steps [t0, t0 + nt) of the sequence: h0 is the state before step t0 and
+  // hn receives the state after step t0 + nt - 1 (a time chunk of a longer
+  // sequence when nt < T; every row index still uses the full T).
+  int t0, nt;
 };
 
 // R = batch rows per GEMV sub-chunk (= rows per cluster when that is <= 8).
@@ -183,6 +187,7 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
   const int warp = tid >> 5, lane = tid & 31;
   const int H = g.H, T = g.T, Hc = g.Hc, Kp = g.nw * 32, bcp = g.bcp, pd = g.pd;
   const int ldg = (3 * H + 3) & ~3;  // row stride of G
+  const int t0 = a.t0, nT = a.nt;  // this launch's steps
   const int j0 = c * Hc;
   const int hcnt = max(1, min(Hc, H - j0));
   // first pointwise item of this thread (row, unit) in a sub-chunk
@@ -232,7 +237,7 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
     mbar_init(bar0, 1);
     mbar_init(bar0 + 8, 1);
     fence_mbar_init();
-    if (T > 1) mbar_expect_tx(bar0 + 8, bytes_per_step);  // slot 1 <- step 1
+    if (nT > 1) mbar_expect_tx(bar0 + 8, bytes_per_step);  // slot 1 <- step 1
   }
 
   // Prefetch of step s's input gates into ring slot s % pd by the threads
@@ -241,7 +246,7 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
   const bool vec4 = g.vec4 != 0;
   auto issue = [&](int s, int first, int stride) {
     float* dst = ring + (s % pd) * ring_stride;
-    const float* src = a.G + ((size_t)b_begin * T + s) * ldg + j0;
+    const float* src = a.G + ((size_t)b_begin * T + t0 + s) * ldg + j0;
     const size_t bstride = (size_t)T * ldg;
     if (vec4) {
       const int h4 = hcnt >> 2, n = nb * 3 * h4;
@@ -260,7 +265,7 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
     }
   };
   for (int s = 0; s < pd - 1; ++s) {
-    if (s < T) issue(s, tid, nthr);
+    if (s < nT) issue(s, tid, nthr);
     cp_async_commit();
   }
   // In the time loop the same threads issue the same copies every step (the
@@ -310,7 +315,7 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
       return;
     }
     float* dst = ring + (s % pd) * ring_stride;
-    const float* src = G_c + (size_t)s * ldg;
+    const float* src = G_c + (size_t)(t0 + s) * ldg;
 #pragma unroll
     for (int k = 0; k < kPlanItems; ++k) {
       if (k < plan_n) {
@@ -330,14 +335,15 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
   cluster.sync();  // buffers and mbarriers of every CTA initialised
 
   bool ok = true;
-  for (int t = 0; t < T; ++t) {
-    const int cur = t & 1, nxt = cur ^ 1;
+  for (int it = 0; it < nT; ++it) {
+    const int t = t0 + it;  // absolute step (row index); `it` counts this launch's steps
+    const int cur = it & 1, nxt = cur ^ 1;
     const float* hcur = hbuf + cur * slot_stride;
-    const float* rg = ring + (t % pd) * ring_stride;
+    const float* rg = ring + (it % pd) * ring_stride;
     // After an expired wait (recorded in the status word) this thread stops
     // waiting but still runs every remaining barrier, so no thread of the CTA
     // or cluster is left behind at one; the results are then invalid.
-    if (t > 0 && ok) ok = mbar_wait_bounded(bar0 + 8 * cur, phase_parity(t));
+    if (it > 0 && ok) ok = mbar_wait_bounded(bar0 + 8 * cur, phase_parity(it));
 
     for (int b0 = 0; b0 < nb; b0 += R) {
       float2 acc[R][3];
@@ -374,7 +380,7 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
       __syncthreads();
       // Every thread is past its wait on slot `cur`: re-arm it for step t+2.
       // (the last thread: it has no pointwise item when R * hcnt < nthr)
-      if (b0 == 0 && tid == nthr - 1 && t + 2 < T) mbar_expect_tx(bar0 + 8 * cur, bytes_per_step);
+      if (b0 == 0 && tid == nthr - 1 && it + 2 < nT) mbar_expect_tx(bar0 + 8 * cur, bytes_per_step);
 
       const int ns = min(R, nb - b0);
       // Threads without a pointwise item in the last sub-chunk issue the
@@ -383,7 +389,7 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
       // sent its step t-1 values, each of which depended on its reads of that
       // slot).
       const int nact = ns * hcnt;
-      if (b0 + R >= nb && idle_issue && tid >= nact && t + pd - 1 < T) issue_step(t + pd - 1);
+      if (b0 + R >= nb && idle_issue && tid >= nact && it + pd - 1 < nT) issue_step(it + pd - 1);
       for (int e = tid; e < ns * hcnt; e += nthr) {
         const int s = e == tid ? my_s : e / hcnt, jl = e == tid ? my_jl : e - s * hcnt;
         const int b = b0 + s, j = j0 + jl;
@@ -398,7 +404,7 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
         const float n = tanhf(gi[2 * Hc] + r * an);
         const float hp = hcur[b * Kp + j];
         const float hnew = n + z * (hp - n);
-        if (t + 1 < T) {
+        if (it + 1 < nT) {
           const uint32_t la = hbuf_u32 + 4u * (uint32_t)(nxt * slot_stride + b * Kp + j);
           const uint32_t lb = bar0 + 8u * nxt;
           for (int q = 0; q < g.C; ++q) st_async_f32(mapa_u32(la, q), hnew, mapa_u32(lb, q));
@@ -413,12 +419,12 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
           st[3 * H] = an;
           st[4 * H] = hp;
         }
-        if (t == T - 1) a.hn[(size_t)(b_begin + b) * H + j] = hnew;
+        if (it == nT - 1) a.hn[(size_t)(b_begin + b) * H + j] = hnew;
       }
       if (b0 + R < nb) __syncthreads();  // `part` is reused by the next sub-chunk
     }
     // Every thread had a pointwise item: prefetch now, after the sends.
-    if (!idle_issue && t + pd - 1 < T) issue_step(t + pd - 1);
+    if (!idle_issue && it + pd - 1 < nT) issue_step(it + pd - 1);
     cp_async_commit();
   }
   cp_async_wait<0>();
@@ -445,6 +451,9 @@ struct BwdArgs {
   // (cols [0, 3H): dG_ih's r, z, n columns; [3H, 4H): dG_hh's n block),
   // accumulated on chip in FP64 over every (b, t) of the cluster.
   double* dbpart;
+  // Steps [t0, t0 + nt), walked backwards: dhn is the gradient flowing into
+  // step t0 + nt - 1 and dh0 receives the gradient of the state before t0.
+  int t0, nt;
 };
 
 template <int R>
@@ -513,8 +522,9 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
   // first, first + stride, ...; 16-byte copies when rows are 16-byte aligned.
   // No commit.
   const bool vec4 = g.vec4 != 0;
+  const int t0 = a.t0, nT = a.nt;
   auto issue = [&](int it, int first, int stride) {
-    const int s = T - 1 - it;
+    const int s = t0 + nT - 1 - it;
     float* dst = ring + (it % pd) * ring_stride;
     const int w = vec4 ? 4 : 1;
     const int hw = hcnt / w, n = nb * 6 * hw;
@@ -535,7 +545,7 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
     }
   };
   for (int it = 0; it < pd - 1; ++it) {
-    if (it < T) issue(it, tid, nthr);
+    if (it < nT) issue(it, tid, nthr);
     cp_async_commit();
   }
   // Per-thread plan of the time loop's prefetch copies (as in the forward).
@@ -582,7 +592,7 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
       issue(it, pfirst, pstride);
       return;
     }
-    const int s = T - 1 - it;
+    const int s = t0 + nT - 1 - it;
     float* dst = ring + (it % pd) * ring_stride;
     const float* src_d = dout_c + (size_t)s * H;
     const float* src_s = stash_c + (size_t)s * 5 * H;
@@ -611,8 +621,8 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
   cluster.sync();
 
   bool ok = true;
-  for (int it = 0; it < T; ++it) {
-    const int t = T - 1 - it;
+  for (int it = 0; it < nT; ++it) {
+    const int t = t0 + nT - 1 - it;
     const float* rg = ring + (it % pd) * ring_stride;
     const int rslot = (it + 1) & 1;  // partials written at iteration it-1
     const float* rin = red + rslot * red_slot;
@@ -632,7 +642,7 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
       // (it-1) % pd: past this iteration's wait every CTA has sent its
       // iteration it-1 partials, which follow (barrier) its reads of the slot).
       const int nact = ns * hcnt;
-      if (b0 + R >= nb && idle_issue && tid >= nact && it + pd - 1 < T) issue_step(it + pd - 1);
+      if (b0 + R >= nb && idle_issue && tid >= nact && it + pd - 1 < nT) issue_step(it + pd - 1);
       for (int e = tid; e < ns * hcnt; e += nthr) {
         const int s = e == tid ? my_s : e / hcnt, jl = e == tid ? my_jl : e - s * hcnt;
         const int b = b0 + s, j = j0 + jl;
@@ -676,8 +686,8 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
       __syncthreads();
       // Every thread has consumed slot `rslot`: re-arm it for iteration it+2
       // (iteration T is the final dh0 read below).
-      if (b0 == 0 && tid == 0 && it > 0 && it + 2 <= T) mbar_expect_tx(bar0 + 8 * rslot, bytes_per_step);
-      if (b0 == 0 && tid == 0 && it == 0 && T >= 2) mbar_expect_tx(bar0 + 8, bytes_per_step);
+      if (b0 == 0 && tid == 0 && it > 0 && it + 2 <= nT) mbar_expect_tx(bar0 + 8 * rslot, bytes_per_step);
+      if (b0 == 0 && tid == 0 && it == 0 && nT >= 2) mbar_expect_tx(bar0 + 8, bytes_per_step);
 
       {
         const uint32_t dst = dst_base + 4u * (uint32_t)(wslot * red_slot + b0 * Hc);
@@ -721,15 +731,15 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
       }
     }
     // Every thread had a pointwise item: prefetch now, after the sends.
-    if (!idle_issue && it + pd - 1 < T) issue_step(it + pd - 1);
+    if (!idle_issue && it + pd - 1 < nT) issue_step(it + pd - 1);
     cp_async_commit();
   }
 
-  // dh0 = g*z of iteration T-1 (t = 0) plus every CTA's partial product of
-  // that iteration, which arrive in slot (T+1)&1.
-  if (ok && T > 0) {
-    const int rslot = (T + 1) & 1;
-    ok = mbar_wait_bounded(bar0 + 8 * rslot, phase_parity(T));
+  // dh0 = g*z of the last iteration (t = t0) plus every CTA's partial product of
+  // that iteration, which arrive in slot (nt+1)&1.
+  if (ok && nT > 0) {
+    const int rslot = (nT + 1) & 1;
+    ok = mbar_wait_bounded(bar0 + 8 * rslot, phase_parity(nT));
     if (ok) {
       const float* rin = red + rslot * red_slot;
       for (int e = tid; e < nb * hcnt; e += nthr) {
@@ -889,6 +899,23 @@ int finish_geometry(RecGeom* g, int device, bool fwd, SmemFn smem_of) {
   return GRU_OK;
 }
 
+// Highest stream priority of the device (numerically smallest).  The time
+// loops launch at this priority so that, when a tensor-core product on a side
+// stream becomes ready at the same moment, the loop's clusters are placed
+// first and the product takes the SMs they leave idle.
+int top_priority() {
+  static int prio = 1;
+  if (prio == 1) {
+    int least = 0, greatest = 0;
+    if (cudaDeviceGetStreamPriorityRange(&least, &greatest) != cudaSuccess) {
+      cudaGetLastError();
+      greatest = 0;
+    }
+    prio = greatest;
+  }
+  return prio;
+}
+
 template <typename Args>
 int launch_clusters(const void* kernel, const Args& a, const RecGeom& g, cudaStream_t stream, int kind) {
   cudaLaunchConfig_t cfg = {};
@@ -896,13 +923,15 @@ int launch_clusters(const void* kernel, const Args& a, const RecGeom& g, cudaStr
   cfg.blockDim = dim3(32 * g.nw, 1, 1);
   cfg.dynamicSmemBytes = g.smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = g.C;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributePriority;
+  attr[1].val.priority = top_priority();
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   Args args = a;
   RecGeom geom = g;
   void* params[2] = {&args, &geom};
@@ -955,12 +984,17 @@ int rec_backward_geometry(int B, int T, int H, int device, RecGeom* g) {
 
 int launch_rec_forward(const float* G, int ldg, const float* h0, const float* w_hh, const float* b_hh,
                        float* out, float* hn, float* stash, const RecGeom& g,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, int t0, int nt) {
   if (ldg != ((3 * g.H + 3) & ~3)) {
     set_error("internal: input-gate row stride must be 3H rounded up to 4");
     return GRU_ERR_INVALID;
   }
-  FwdArgs a{G, h0, w_hh, b_hh, out, hn, stash};
+  if (nt < 0) nt = g.T;
+  if (t0 < 0 || nt < 1 || t0 + nt > g.T) {
+    set_error("internal: time window outside the sequence");
+    return GRU_ERR_INVALID;
+  }
+  FwdArgs a{G, h0, w_hh, b_hh, out, hn, stash, t0, nt};
   RecGeom gg = g;
   if (reinterpret_cast<uintptr_t>(G) & 15) gg.vec4 = 0;  // 16-byte copies need an aligned base
   return launch_clusters(kernel_for(true, gg.R), a, gg, stream, kKindFwdRecurrent);
@@ -968,8 +1002,14 @@ int launch_rec_forward(const float* G, int ldg, const float* h0, const float* w_
 
 int launch_rec_backward(const float* dout, const float* dhn, const float* w_hh,
                         const float* stash, float* dGi, float* dGi_lo, int ldgi, float* dGh, float* dGh_lo,
-                        int ldgn, float* dh0, double* dbpart, const RecGeom& g, cudaStream_t stream) {
-  BwdArgs a{dout, dhn, w_hh, stash, dGi, dGi_lo, ldgi, dGh, dGh_lo, ldgn, dh0, dbpart};
+                        int ldgn, float* dh0, double* dbpart, const RecGeom& g, cudaStream_t stream, int t0,
+                        int nt) {
+  if (nt < 0) nt = g.T;
+  if (t0 < 0 || nt < 1 || t0 + nt > g.T) {
+    set_error("internal: time window outside the sequence");
+    return GRU_ERR_INVALID;
+  }
+  BwdArgs a{dout, dhn, w_hh, stash, dGi, dGi_lo, ldgi, dGh, dGh_lo, ldgn, dh0, dbpart, t0, nt};
   RecGeom gg = g;
   if ((reinterpret_cast<uintptr_t>(dout) | reinterpret_cast<uintptr_t>(stash)) & 15) gg.vec4 = 0;
   return launch_clusters(kernel_for(false, gg.R), a, gg, stream, kKindBwdRecurrent);
