@@ -264,6 +264,14 @@ def load_traffic():
 # ---------------------------------------------------------------------------
 # timing helpers
 # ---------------------------------------------------------------------------
+# Set in main() when several ranks run: a tiny all-reduce that lines the
+# ranks' GPUs up after the pre-timing device sleep (outside every event
+# window).  Without it, a rank whose host reached the timed region later (rank
+# 0 waits for its clock sampler's first sample) made the first all-reduce of
+# the other ranks wait for it inside their first timed step.
+ALIGN_RANKS = None
+
+
 def timed_steps(step_fn, K, flush, torch):
     """Per-step device times (ms).  A device-side sleep first lets the host
     enqueue the K steps ahead of the GPU, so a host-side stall while
@@ -274,6 +282,8 @@ def timed_steps(step_fn, K, flush, torch):
     sleep = getattr(torch.cuda, "_sleep", None)
     if sleep is not None:
         sleep(int(30e-3 * 1.965e9))  # ~30 ms of device cycles
+    if ALIGN_RANKS is not None:
+        ALIGN_RANKS()
     for k in range(K):
         flush()
         evs[k][0].record()
@@ -321,6 +331,8 @@ def strong_scaling(args, world, rank, dev, K, W, flush, barrier, torch, dist):
         graph = GraphedTrainStep(trainer, [(x, y)], warmup=1,
                                  capture_error_mode="thread_local" if world > 1 else "global",
                                  include_update=world == 1)
+        for _ in range(W):  # untimed replays (the first one uploads the graph)
+            graph.step(0)
     barrier()
     torch.cuda.synchronize()
     times = timed_steps((lambda k: graph.step(0)) if graph else (lambda k: trainer.step(x, y)), K, flush, torch)
@@ -457,6 +469,9 @@ def main():
     dev = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
+        global ALIGN_RANKS
+        _align = torch.zeros(1, device=dev)
+        ALIGN_RANKS = lambda: dist.all_reduce(_align)  # noqa: E731
 
     from rnn_kernel_b200 import GRU, DataParallelTrainer, GraphedTrainStep, _lib
 
@@ -516,6 +531,10 @@ def main():
             graph = None
             graph_error = f"{type(exc).__name__}: {exc}"[:200]
     graphed = graph is not None
+    if graph is not None:
+        # untimed replays: the first launch of an instantiated graph uploads it
+        for _ in range(W):
+            graph.step(0)
     barrier()
     torch.cuda.synchronize()
     # only rank 0 reports clocks: the other ranks do not poll NVML (8 processes
@@ -616,6 +635,7 @@ def main():
         if world > 1:
             dist.destroy_process_group()
         return 0
+    ALIGN_RANKS = None  # rank 0 alone from here on (cuDNN and CPU comparisons)
 
     # ---- kernel roofline (dominant kernel, measured live in the timed region) ----
     per_kind = {k: {"ms_per_launch": (tot / n if n else None), "launches": n, "ms_per_step": tot / K}
@@ -662,7 +682,7 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": ms, "median_ms_per_step": st["p50"], "p90_ms_per_step": st["p90"],
-        "max_ms_per_step": st["max"], "higher_is_better": True,
+        "max_ms_per_step": st["max"], "step_ms_rank0": [round(t, 4) for t in times], "higher_is_better": True,
         "graph": graphed, "eager_ms_per_step": est["mean"], "eager_median_ms_per_step": est["p50"],
         "scaling": scaling, "vs_baseline": None,
         "dtype": "fp32", "data": "synthetic: x, target ~ N(0,1) per rank (seed 1000+rank); weights U(-1/16,1/16)",
