@@ -205,7 +205,25 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
   // W_hh rows (r, z, n) of unit j0+lane, columns [32*warp, 32*warp+32), as
   // pairs of consecutive columns for FFMA2.
   float2 wr[16], wz[16], wn[16];
-  {
+  if (H % 4 == 0 && (reinterpret_cast<uintptr_t>(a.w_hh) & 15) == 0) {
+    // The 32 columns of a row this thread holds are contiguous: 8 16-byte
+    // loads per gate (the scalar loads below, lanes on 32 different rows,
+    // made this prologue ~16 us, a cost paid by every launch).
+    const int jg = j0 + lane;
+    const bool jv = lane < hcnt && jg < H;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int k = warp * 32 + 4 * q;
+      const bool v = jv && k < H;  // H % 4 == 0: a 16-byte piece is wholly inside or outside
+      const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 r = v ? *reinterpret_cast<const float4*>(a.w_hh + (size_t)jg * H + k) : zero;
+      const float4 z = v ? *reinterpret_cast<const float4*>(a.w_hh + (size_t)(H + jg) * H + k) : zero;
+      const float4 n = v ? *reinterpret_cast<const float4*>(a.w_hh + (size_t)(2 * H + jg) * H + k) : zero;
+      wr[2 * q] = make_float2(r.x, r.y), wr[2 * q + 1] = make_float2(r.z, r.w);
+      wz[2 * q] = make_float2(z.x, z.y), wz[2 * q + 1] = make_float2(z.z, z.w);
+      wn[2 * q] = make_float2(n.x, n.y), wn[2 * q + 1] = make_float2(n.z, n.w);
+    }
+  } else {
     const int jg = j0 + lane;
     const bool jv = lane < hcnt && jg < H;
 #pragma unroll
