@@ -100,6 +100,23 @@ int gru_forward_inference_noalloc(const float* x, const float* h0, const float* 
                                   const float* w_hh, const float* b_ih, const float* b_hh,
                                   float* out, float* hn, int B, int T, int I, int H, void* stream);
 
+/* ---- MSE loss of the output (the training harness's F.mse_loss(pred, y):
+ * rnn_benchmark.py:636, :657, :680; tests/test_sequence_chunking.py:27-28),
+ * fused into one pass each way instead of torch's three. ---- */
+
+/* Workspace of gru_mse_loss for n elements (FP64 block partials). */
+size_t gru_mse_workspace_bytes(long n);
+
+/* *loss = mean((out - target)^2) over n floats (device pointers; the sum in
+ * FP64, deterministic). */
+int gru_mse_loss(const float* out, const float* target, long n, float* loss, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
+/* dout = (2 / n) * (out - target) * (*grad_loss), grad_loss a device scalar
+ * (the loss's upstream gradient), in torch's order of operations. */
+int gru_mse_loss_backward(const float* out, const float* target, const float* grad_loss, float* dout, long n,
+                          void* stream);
+
 /* Time chunks (no reference counterpart; a scheduling knob of this library).
  * When the time loops leave SMs idle (e.g. 104 of 148 at H = 256, B = 64),
  * gru_forward and gru_backward run the sequence as n consecutive chunks and
@@ -118,7 +135,7 @@ int gru_set_time_chunks(int n);
  * scripts/profile_a100_h256_step.py).  Kernel kinds: 0 input-projection GEMM,
  * 1 forward time loop, 2 backward time loop, 3 gradient products (dW, dx;
  * + split-K reduce), 4 bias-gradient column sums, 5 padding / transpose
- * copies. ---- */
+ * copies, 6 MSE loss and its gradient. ---- */
 
 /* Device status word of the current device: 0 when every kernel so far ran
  * to completion, else GRU_STATUS_* bits (a bounded wait inside a time-loop

@@ -12,6 +12,7 @@ from .gru import (
     is_b200_available,
     is_supported_gru,
 )
+from .loss import MSELossFunction, mse_loss
 from .train import DataParallelTrainer, GraphedTrainStep, HostBatchPrefetcher, flatten_parameters_
 
 B200GRU = GRU
@@ -29,4 +30,6 @@ __all__ = [
     "gru_forward_inference",
     "is_b200_available",
     "is_supported_gru",
+    "mse_loss",
+    "MSELossFunction",
 ]

@@ -39,11 +39,15 @@ SIGNATURES = {
     "gru_selftest_wait_timeout": (_int, [_int, ctypes.c_void_p, ctypes.c_void_p]),
     "gru_launch_count": (ctypes.c_ulonglong, []),
     "gru_set_time_chunks": (_int, [_int]),
+    "gru_mse_workspace_bytes": (_size_t, [ctypes.c_long]),
+    "gru_mse_loss": (_int, [_c_float_p, _c_float_p, ctypes.c_long, _c_float_p, ctypes.c_void_p, _size_t,
+                            ctypes.c_void_p]),
+    "gru_mse_loss_backward": (_int, [_c_float_p, _c_float_p, _c_float_p, _c_float_p, ctypes.c_long, ctypes.c_void_p]),
     "gru_timing_enable": (_int, [_int]),
     "gru_timing_collect": (_int, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int), _int]),
 }
 
-KERNEL_KINDS = ("input_gemm", "fwd_recurrent", "bwd_recurrent", "grad_gemm", "colsum", "layout")
+KERNEL_KINDS = ("input_gemm", "fwd_recurrent", "bwd_recurrent", "grad_gemm", "colsum", "layout", "loss")
 
 
 def timing_enable(on: bool) -> None:

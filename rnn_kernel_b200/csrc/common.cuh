@@ -169,7 +169,8 @@ enum KernelKind {
   kKindGradGemm = 3,    // dW_hh, dW_ih, dx products (+ split-K reduce)
   kKindColsum = 4,      // db_ih / db_hh
   kKindLayout = 5,      // padding / transpose copies feeding the tensor-core products
-  kKindCount = 6
+  kKindLoss = 6,        // MSE loss and its gradient
+  kKindCount = 7
 };
 
 class LaunchScope {
