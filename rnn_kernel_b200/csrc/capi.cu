@@ -446,7 +446,6 @@ int forward_impl(const float* x, const float* h0, const float* w_ih, const float
   float* wl = reinterpret_cast<float*>(ws + l.wl);
   // G = x . W_ih^T + b_ih on the tensor cores (3xTF32, pre-split operands).
   const SplitArgs sp[2] = {{x, (long)B * T, I, I, xh, xl, l.ldx}, {w_ih, 3L * H, I, I, wh, wl, l.ldx}};
-  if ((rc = split_tf32_multi(sp, 2, stream))) return rc;
   TcGemmArgs ga{xh, l.ldx, wh, l.ldx, G, l.ldg, b_ih, B * T, 3 * H, I, false, false, xl, wl};
   RecGeom g{};
   if ((rc = geometry(0, B, T, H, dev, &g))) return rc;
@@ -454,6 +453,7 @@ int forward_impl(const float* x, const float* h0, const float* w_ih, const float
   Side* sd = nullptr;
   if (nch > 1 && (rc = side_stream(dev, stream, &sd))) return rc;
   if (nch == 1 || sd == nullptr) {
+    if ((rc = split_tf32_multi(sp, 2, stream))) return rc;
     if ((rc = tc_gemm(ga, stream, kKindInputGemm))) return rc;
     return launch_rec_forward(G, l.ldg, h0, w_hh, b_hh, out, hn, stash, g, stream);
   }
@@ -472,6 +472,20 @@ int forward_impl(const float* x, const float* h0, const float* w_ih, const float
     a.rstride = T;
     return a;
   };
+  // The split copy of x is made per chunk too (chunk c's rows, periodic like
+  // the projection's), chunk 0's with W_ih's before the first projection.
+  auto split_x = [&](int c) {
+    SplitArgs a = sp[0];
+    a.src = x + (size_t)c * Tc * I;
+    a.hi = xh + (size_t)c * Tc * l.ldx;
+    a.lo = xl + (size_t)c * Tc * l.ldx;
+    a.rows = (long)B * Tc;
+    a.rin = Tc;
+    a.rstride = T;
+    return a;
+  };
+  const SplitArgs sp0[2] = {split_x(0), sp[1]};
+  if ((rc = split_tf32_multi(sp0, 2, stream))) return rc;
   // Every loop is issued before the product that runs beside it, so that
   // the loop's clusters are placed first.
   if ((rc = tc_gemm(chunk(0), stream, kKindInputGemm))) return rc;
@@ -481,6 +495,8 @@ int forward_impl(const float* x, const float* h0, const float* w_ih, const float
       return rc;
     if (c + 1 < nch) {
       if (c == 0) GRU_CUDA_TRY(cudaStreamWaitEvent(sd->s, sd->fork, 0));
+      const SplitArgs spc = split_x(c + 1);
+      if ((rc = split_tf32_multi(&spc, 1, sd->s))) return rc;
       if ((rc = tc_gemm(chunk(c + 1), sd->s, kKindInputGemm, nullptr, 0, free))) return rc;
       if ((rc = stream_after(stream, sd->s, sd->join))) return rc;  // the loop over chunk c+1 needs it
     }

@@ -111,6 +111,10 @@ struct SplitArgs {
   float* hi;
   float* lo;
   int ldd;
+  // Periodic rows (as TcGemmArgs::rin): logical row r of src and of hi / lo
+  // is physical row (r / rin) * rstride + r % rin; rin = 0: plain rows.
+  int rin = 0;
+  long rstride = 0;
 };
 int split_tf32_multi(const SplitArgs* a, int n, cudaStream_t stream);
 bool tc_gemm_supported(const TcGemmArgs& a);

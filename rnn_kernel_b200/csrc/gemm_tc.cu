@@ -637,6 +637,8 @@ struct SplitJob {
   float* lo;
   long rows, lds, row_end;  // row_end: cumulative rows over the launch
   int cols, ldd, vec;       // vec: float4 path allowed
+  int rin;                  // periodic rows (0: plain)
+  long rstride;
 };
 struct SplitJobs {
   SplitJob j[4];
@@ -651,7 +653,8 @@ __global__ void split_tf32_kernel(const __grid_constant__ SplitJobs js) {
     int ji = 0;
     while (ji + 1 < js.n && g >= js.j[ji].row_end) ++ji;
     const SplitJob& J = js.j[ji];
-    const long r = g - (ji > 0 ? js.j[ji - 1].row_end : 0);
+    const long rl = g - (ji > 0 ? js.j[ji - 1].row_end : 0);
+    const long r = J.rin > 0 ? (rl / J.rin) * J.rstride + rl % J.rin : rl;
     const float* sr = J.src + r * J.lds;
     float* hr = J.hi + r * J.ldd;
     float* lr = J.lo + r * J.ldd;
@@ -695,6 +698,8 @@ int split_tf32_multi(const SplitArgs* a, int n, cudaStream_t stream) {
     J.lds = a[i].lds;
     J.cols = a[i].cols;
     J.ldd = a[i].ldd;
+    J.rin = a[i].rin;
+    J.rstride = a[i].rstride;
     J.vec = (a[i].cols % 4 == 0 && a[i].lds % 4 == 0 && a[i].ldd % 4 == 0 &&
              ((reinterpret_cast<uintptr_t>(a[i].src) | reinterpret_cast<uintptr_t>(a[i].hi) |
                reinterpret_cast<uintptr_t>(a[i].lo)) & 15) == 0) ? 1 : 0;

@@ -140,6 +140,9 @@ class GRUFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, h0, weight_ih, weight_hh, bias_ih, bias_hh):
         out, hn, stash, (xc, w_ih, w_hh) = _forward_impl(x, h0, weight_ih, weight_hh, bias_ih, bias_hh, True)
+        # an output the loss does not use arrives as None (the C ABI takes NULL
+        # for it) instead of a materialised zero tensor
+        ctx.set_materialize_grads(False)
         ctx.save_for_backward(xc, w_ih, w_hh, stash if stash is not None else out.new_empty(0))
         ctx.shape = (x.size(0), x.size(1), x.size(2), h0.size(1))
         return out, hn
