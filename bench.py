@@ -66,6 +66,9 @@ def parse():
     ap.add_argument("--no-dp-check", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the cuDNN comparison sweep")
     ap.add_argument("--no-graph", action="store_true", help="eager steps only (no CUDA graph replay)")
+    ap.add_argument("--timeline", action="store_true",
+                    help="profiling only: use the instrumented library build and add the time loops' per-phase "
+                         "step timeline (clock64 cycles) to the line; its step times are not bench values")
     ap.add_argument("--time-chunks", type=int, default=0,
                     help="time chunks of the forward/backward (0 automatic, 1 off, 2..4 forced where possible)")
     return ap.parse_args()
@@ -293,6 +296,33 @@ def timed_steps(step_fn, K, flush, torch):
     return [a.elapsed_time(b) for a, b in evs]
 
 
+def step_timeline(lib):
+    """Per-phase cycles of the time loops from the instrumented build: for each
+    loop, CTA 0 / thread 0 (which has a pointwise item) and CTA 0's last
+    thread (an input-prefetch issuer when the last sub-chunk leaves threads
+    idle), the median over 8 consecutive steps of each point's clock64 offset
+    from the step start, and the median step length in cycles."""
+    import numpy as np
+
+    buf = lib.timeline_read()
+    out = {"source": "clock64 at marked points of steps 100-107 of the last launch of each loop "
+                     "(instrumented build, RNN_KERNEL_B200_VARIANT=timeline)"}
+    for d, name in enumerate(("fwd", "bwd")):
+        pts = lib.TIMELINE_POINTS[name]
+        rec = {}
+        for w, who in ((0, "cta0_thread0"), (1, "cta0_last_thread")):
+            tl = buf[d, w]
+            steps = np.diff(tl[:, 0])
+            ph = {}
+            for k, pn in enumerate(pts):
+                col = tl[:, k]
+                if np.all(col != 0):
+                    ph[pn] = int(np.median(col - tl[:, 0]))
+            rec[who] = {"step_cycles": int(np.median(steps)) if len(steps) else None, "offsets": ph}
+        out[name] = rec
+    return out
+
+
 def step_stats(times, world, dev, torch, dist):
     """mean / p50 / p90 / max of per-step ms, each the max over ranks."""
     srt = sorted(times)
@@ -460,6 +490,8 @@ def main():
     if args.impl == "reference":
         return run_reference(args, world, rank)
 
+    if args.timeline:  # before the package is imported: it picks its library at import
+        os.environ["RNN_KERNEL_B200_VARIANT"] = "timeline"
     import torch
     import torch.distributed as dist
 
@@ -513,6 +545,7 @@ def main():
     torch.cuda.synchronize()
     barrier()
     est = step_stats(etimes, world, dev, torch, dist)
+    timeline = step_timeline(_lib) if args.timeline else None
 
     # ---- headline: the same step replayed from a CUDA graph ----
     # (zero grads + fwd + loss + bwd captured, and at N = 1 the SGD update
@@ -694,6 +727,7 @@ def main():
         "clocks": clocks,
         "gpu_launches": int(launches),
         "kernels": per_kind,
+        **({"timeline": timeline} if timeline is not None else {}),
         "roofline": roofline,
         "step_roofline": step_roof,
         "e2e": e2e,

@@ -84,6 +84,33 @@ def launch_count() -> int:
     return int(load().gru_launch_count())
 
 
+TIMELINE_POINTS = {
+    "fwd": ("step_start", "wait_done", "product_done", "barrier_done", "partials_summed", "gates_done",
+            "sent", "stored", "step_end", "prefetch_issued"),
+    "bwd": ("step_start", "copies_waited", "wait_done", "barrier1_done", "dh_summed", "pointwise_done",
+            "dG_stored", "db_added", "barrier2_done", "product_done", "sent", "step_end"),
+}
+
+
+def timeline_read():
+    """Step timeline of an instrumented build (RNN_KERNEL_B200_VARIANT=timeline):
+    int64 clock64 values [direction (fwd, bwd)][CTA 0 thread 0, CTA 0 last
+    thread, CTA 1 thread 0, CTA 1 last thread][step][point] of the last
+    launch of each time loop (points: TIMELINE_POINTS; 0 = not recorded)."""
+    import numpy as np
+
+    lib = load()
+    fn = getattr(lib, "gru_timeline_read", None)
+    if fn is None:
+        raise RuntimeError("this library was built without the step timeline "
+                           "(set RNN_KERNEL_B200_VARIANT=timeline)")
+    fn.restype = _int
+    fn.argtypes = [ctypes.c_void_p]
+    buf = np.zeros((2, 4, 8, 12), dtype=np.int64)
+    check(fn(buf.ctypes.data), "gru_timeline_read")
+    return buf
+
+
 def library_path() -> Path:
     return _build.LIB_PATH
 

@@ -15,8 +15,16 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
-LIB_NAME = "librnn_kernel_b200.so"
+# RNN_KERNEL_B200_VARIANT=timeline selects an instrumented build of the same
+# sources (-DGRU_TIMELINE: the time loops record clock64() at the phases of a
+# few steps, read back by gru_timeline_read) in a library of its own; it is
+# slower by a few percent and only used for profiling (bench.py --timeline).
+VARIANT = os.environ.get("RNN_KERNEL_B200_VARIANT", "")
+if VARIANT not in ("", "timeline"):
+    raise ValueError(f"RNN_KERNEL_B200_VARIANT must be unset or 'timeline', got {VARIANT!r}")
+LIB_NAME = "librnn_kernel_b200_timeline.so" if VARIANT else "librnn_kernel_b200.so"
 LIB_PATH = PKG / LIB_NAME
+VARIANT_FLAGS = ["-DGRU_TIMELINE"] if VARIANT == "timeline" else []
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -49,7 +57,7 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
     if not force and not needs_build():
         return LIB_PATH
     tmp = LIB_PATH.with_suffix(".so.tmp")
-    cmd = [nvcc_path(), *NVCC_FLAGS, *(extra or []), "-I", str(ROOT / "include"),
+    cmd = [nvcc_path(), *NVCC_FLAGS, *VARIANT_FLAGS, *(extra or []), "-I", str(ROOT / "include"),
            *map(str, sources()), "-o", str(tmp)]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)

@@ -46,6 +46,25 @@ namespace gru {
 
 __device__ int g_device_status = 0;
 
+#ifdef GRU_TIMELINE
+// Step timeline, compiled only into instrumented builds (-DGRU_TIMELINE):
+// clock64() at marked points of iterations [kTlIt0, kTlIt0 + kTlSteps) of
+// every launch, for threads 0 and blockDim-1 of the first two CTAs of
+// cluster 0 (the last launch of each direction wins).
+constexpr int kTlIt0 = 100, kTlSteps = 8, kTlPts = 12;
+__device__ long long g_tl[2][4][kTlSteps][kTlPts];
+#define GRU_TL(dir, k)                                                                              \
+  do {                                                                                              \
+    if (blockIdx.x < 2 && (threadIdx.x == 0 || threadIdx.x == blockDim.x - 1) && it >= kTlIt0 &&    \
+        it < kTlIt0 + kTlSteps)                                                                     \
+      g_tl[dir][blockIdx.x * 2 + (threadIdx.x != 0)][it - kTlIt0][k] = clock64();                   \
+  } while (0)
+#else
+#define GRU_TL(dir, k) \
+  do {                 \
+  } while (0)
+#endif
+
 namespace {
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
@@ -358,10 +377,12 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
     const int cur = it & 1, nxt = cur ^ 1;
     const float* hcur = hbuf + cur * slot_stride;
     const float* rg = ring + (it % pd) * ring_stride;
+    GRU_TL(0, 0);
     // After an expired wait (recorded in the status word) this thread stops
     // waiting but still runs every remaining barrier, so no thread of the CTA
     // or cluster is left behind at one; the results are then invalid.
     if (it > 0 && ok) ok = mbar_wait_bounded(bar0 + 8 * cur, phase_parity(it));
+    GRU_TL(0, 1);
 
     for (int b0 = 0; b0 < nb; b0 += R) {
       float2 acc[R][3];
@@ -387,6 +408,7 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
       // the 32 lanes hit 32 distinct banks, and the pointwise thread reads its
       // unit's 8 partials with two float4 loads that are contiguous across
       // lanes (4 wavefronts each).
+      if (b0 == 0) GRU_TL(0, 2);
       const int slot = (warp + (lane >> 3)) & 7;
       float* pw = part + ((slot >> 2) * 32 + lane) * 4 + (slot & 3);
 #pragma unroll
@@ -396,6 +418,7 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
       }
       if (b0 == 0) cp_async_wait_dyn(pd - 2);
       __syncthreads();
+      if (b0 == 0) GRU_TL(0, 3);
       // Every thread is past its wait on slot `cur`: re-arm it for step t+2.
       // (the last thread: it has no pointwise item when R * hcnt < nthr)
       if (b0 == 0 && tid == nthr - 1 && it + 2 < nT) mbar_expect_tx(bar0 + 8 * cur, bytes_per_step);
@@ -408,6 +431,7 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
       // slot).
       const int nact = ns * hcnt;
       if (b0 + R >= nb && idle_issue && tid >= nact && it + pd - 1 < nT) issue_step(it + pd - 1);
+      if (b0 + R >= nb) GRU_TL(0, 9);
       for (int e = tid; e < ns * hcnt; e += nthr) {
         const int s = e == tid ? my_s : e / hcnt, jl = e == tid ? my_jl : e - s * hcnt;
         const int b = b0 + s, j = j0 + jl;
@@ -416,17 +440,20 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
         const float ar = bsl[jl] + (((r0.x + r0.y) + (r0.z + r0.w)) + ((r1.x + r1.y) + (r1.z + r1.w)));
         const float az = bsl[Hc + jl] + (((z0.x + z0.y) + (z0.z + z0.w)) + ((z1.x + z1.y) + (z1.z + z1.w)));
         const float an = bsl[2 * Hc + jl] + (((n0.x + n0.y) + (n0.z + n0.w)) + ((n1.x + n1.y) + (n1.z + n1.w)));
+        if (e == tid && b0 == 0) GRU_TL(0, 4);
         const float* gi = rg + (b * 3) * Hc + jl;
         const float r = sigmoidf_acc(gi[0] + ar);
         const float z = sigmoidf_acc(gi[Hc] + az);
         const float n = tanhf(gi[2 * Hc] + r * an);
         const float hp = hcur[b * Kp + j];
         const float hnew = n + z * (hp - n);
+        if (e == tid && b0 == 0) GRU_TL(0, 5);
         if (it + 1 < nT) {
           const uint32_t la = hbuf_u32 + 4u * (uint32_t)(nxt * slot_stride + b * Kp + j);
           const uint32_t lb = bar0 + 8u * nxt;
           for (int q = 0; q < g.C; ++q) st_async_f32(mapa_u32(la, q), hnew, mapa_u32(lb, q));
         }
+        if (e == tid && b0 == 0) GRU_TL(0, 6);
         const size_t row = (size_t)(b_begin + b) * T + t;
         a.out[row * H + j] = hnew;
         if (a.stash != nullptr) {
@@ -438,12 +465,14 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
           st[4 * H] = hp;
         }
         if (it == nT - 1) a.hn[(size_t)(b_begin + b) * H + j] = hnew;
+        if (e == tid && b0 == 0) GRU_TL(0, 7);
       }
       if (b0 + R < nb) __syncthreads();  // `part` is reused by the next sub-chunk
     }
     // Every thread had a pointwise item: prefetch now, after the sends.
     if (!idle_issue && it + pd - 1 < nT) issue_step(it + pd - 1);
     cp_async_commit();
+    GRU_TL(0, 8);
   }
   cp_async_wait<0>();
   cluster.sync();  // no CTA leaves while a peer may still write into it
@@ -645,15 +674,19 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
     const int rslot = (it + 1) & 1;  // partials written at iteration it-1
     const float* rin = red + rslot * red_slot;
     const int wslot = it & 1;
+    GRU_TL(1, 0);
     // This thread's ring copies for iteration it (visible to all after the
     // barrier below); waited for before the partials, whose wait absorbs it.
     cp_async_wait_dyn(pd - 2);
+    GRU_TL(1, 1);
     // After an expired wait (recorded in the status word) this thread stops
     // waiting but still runs every remaining barrier; results are then invalid.
     if (it > 0 && ok) ok = mbar_wait_bounded(bar0 + 8 * rslot, phase_parity(it));
+    GRU_TL(1, 2);
 
     for (int b0 = 0; b0 < nb; b0 += R) {
       __syncthreads();
+      if (b0 == 0) GRU_TL(1, 3);
       const int ns = min(R, nb - b0);
       // Threads without a pointwise item in the last sub-chunk issue the
       // prefetch for iteration it+pd-1 meanwhile (it overwrites ring slot
@@ -675,6 +708,7 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
 #pragma unroll
           for (int q = 0; q < kMaxCluster; ++q) dh += pp[q];
         }
+        if (e == tid && b0 == 0) GRU_TL(1, 4);
         const float* v = rg + (b * 6) * Hc + jl;
         const float gg = dh + v[0];
         const float r = v[Hc], z = v[2 * Hc], n = v[3 * Hc], hn = v[4 * Hc], hp = v[5 * Hc];
@@ -689,19 +723,23 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
         dgs[(s * 3 + 1) * 32 + jl] = dz_pre;
         dgs[(s * 3 + 2) * 32 + jl] = dhn_gate;
         gz[b * Hc + jl] = gg * z;
+        if (e == tid && b0 == 0) GRU_TL(1, 5);
         const size_t row = (size_t)(b_begin + b) * T + t;
         const size_t o = row * a.ldgi + j, on = row * a.ldgn + j;
         split_store(a.dGi + o, a.dGi_lo + o, dr_pre);
         split_store(a.dGi + o + H, a.dGi_lo + o + H, dz_pre);
         split_store(a.dGi + o + 2 * H, a.dGi_lo + o + 2 * H, dn_pre);
         split_store(a.dGh + on, a.dGh_lo + on, dhn_gate);
+        if (e == tid && b0 == 0) GRU_TL(1, 6);
         double* acc = dbacc + (s * 4) * Hc + jl;
         acc[0] += (double)dr_pre;
         acc[Hc] += (double)dz_pre;
         acc[2 * Hc] += (double)dn_pre;
         acc[3 * Hc] += (double)dhn_gate;
+        if (e == tid && b0 == 0) GRU_TL(1, 7);
       }
       __syncthreads();
+      if (b0 == 0) GRU_TL(1, 8);
       // Every thread has consumed slot `rslot`: re-arm it for iteration it+2
       // (iteration T is the final dh0 read below).
       if (b0 == 0 && tid == 0 && it > 0 && it + 2 <= nT) mbar_expect_tx(bar0 + 8 * rslot, bytes_per_step);
@@ -735,6 +773,7 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
             acc[s][2] = __ffma2_rn(make_float2(vn.w, vn.w), wn[jj + 3], acc[s][2]);
           }
         }
+        if (b0 == 0) GRU_TL(1, 9);
 #pragma unroll
         for (int s = 0; s < R; ++s) {
           // this half's sums for columns k0 and k0+1; the other half (lane ^ 16)
@@ -746,11 +785,13 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
           const float v = jh == 0 ? c0 + o0 : o1 + c1;  // column ksend = k0 + jh
           if (s < ns && ksend < H) st_async_f32(dst + 4u * (uint32_t)(s * Hc), v, dbar);
         }
+        if (b0 == 0) GRU_TL(1, 10);
       }
     }
     // Every thread had a pointwise item: prefetch now, after the sends.
     if (!idle_issue && it + pd - 1 < nT) issue_step(it + pd - 1);
     cp_async_commit();
+    GRU_TL(1, 11);
   }
 
   // dh0 = g*z of the last iteration (t = t0) plus every CTA's partial product of
@@ -980,6 +1021,14 @@ int wait_probe(unsigned long long limit_ns, int* result_dev, cudaStream_t stream
   return GRU_OK;
 }
 
+#ifdef GRU_TIMELINE
+int read_timeline(long long* out) {
+  GRU_CUDA_TRY(cudaDeviceSynchronize());
+  GRU_CUDA_TRY(cudaMemcpyFromSymbol(out, g_tl, sizeof(g_tl)));
+  return GRU_OK;
+}
+#endif
+
 int read_device_status(int reset, int* status) {
   GRU_CUDA_TRY(cudaDeviceSynchronize());
   GRU_CUDA_TRY(cudaMemcpyFromSymbol(status, g_device_status, sizeof(int)));
@@ -1034,3 +1083,9 @@ int launch_rec_backward(const float* dout, const float* dhn, const float* w_hh,
 }
 
 }  // namespace gru
+
+#ifdef GRU_TIMELINE
+// Instrumented builds only: copies the step timeline (int64 clock64 values,
+// [direction 2][CTA 0/1 x thread 0/last 4][step 8][point 12]) to out.
+extern "C" int gru_timeline_read(long long* out) { return gru::read_timeline(out); }
+#endif
