@@ -130,6 +130,16 @@ int gru_mse_loss_backward(const float* out, const float* target, const float* gr
  * setting, or -1 for an invalid n. */
 int gru_set_time_chunks(int n);
 
+/* Time-loop kernels for small hidden sizes (no reference counterpart; a
+ * kernel-selection knob of this library).  mode 0 (default): the forward
+ * time loop for H <= 96 and the backward one for H <= 32 run one CTA per
+ * group of up to 4 batch rows, which holds all of W_hh and runs a step with
+ * one barrier; mode 1: the thread-block-cluster kernels used for larger H,
+ * everywhere.  Both compute the same function (results agree to FP32
+ * rounding).  Process-wide; returns the previous mode, or -1 for an invalid
+ * mode. */
+int gru_set_small_loops(int mode);
+
 /* ---- Telemetry (no reference counterpart: the reference had no kernel
  * timers; its profiling scripts used torch.profiler / nsys, see
  * scripts/profile_a100_h256_step.py).  Kernel kinds: 0 input-projection GEMM,

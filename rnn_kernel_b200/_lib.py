@@ -39,6 +39,7 @@ SIGNATURES = {
     "gru_selftest_wait_timeout": (_int, [_int, ctypes.c_void_p, ctypes.c_void_p]),
     "gru_launch_count": (ctypes.c_ulonglong, []),
     "gru_set_time_chunks": (_int, [_int]),
+    "gru_set_small_loops": (_int, [_int]),
     "gru_mse_workspace_bytes": (_size_t, [ctypes.c_long]),
     "gru_mse_loss": (_int, [_c_float_p, _c_float_p, ctypes.c_long, _c_float_p, ctypes.c_void_p, _size_t,
                             ctypes.c_void_p]),
@@ -77,6 +78,15 @@ def set_time_chunks(n: int) -> int:
     prev = load().gru_set_time_chunks(int(n))
     if prev < 0:
         raise ValueError(f"time chunks must be 0..4, got {n}")
+    return prev
+
+
+def set_small_loops(mode: int) -> int:
+    """Time-loop kernels for H <= 96: 0 single-CTA (default), 1 cluster;
+    returns the previous mode."""
+    prev = load().gru_set_small_loops(int(mode))
+    if prev < 0:
+        raise ValueError(f"small-loops mode must be 0 or 1, got {mode}")
     return prev
 
 

@@ -18,7 +18,7 @@ namespace gru {
 namespace {
 thread_local std::string g_last_error;
 std::mutex g_mu;
-std::map<std::tuple<int, int, int, int>, RecGeom> g_geom;  // (device, kind, B, H)
+std::map<std::tuple<int, int, int, int, int>, RecGeom> g_geom;  // (device, kind, B, H, small-loops mode)
 std::map<int, int> g_sms;
 
 constexpr size_t kAlign = 256;
@@ -48,7 +48,7 @@ constexpr double kBoundarySeconds = 30e-6;
 // over the whole sequence.
 int time_chunks(const RecGeom& g, int device, double side_flops) {
   const int knob = g_time_chunks.load();
-  if (knob == 1) return 1;
+  if (knob == 1 || g.small) return 1;  // the single-CTA loops of small H are too short to hide products
   const int sms = sm_count(device);
   const int free = sms - g.C * g.nclusters;
   if (g.nclusters > g.max_clusters || free < 1) return 1;
@@ -99,7 +99,7 @@ int stream_after(cudaStream_t to, cudaStream_t from, cudaEvent_t ev) {
 int geometry(int kind, int B, int T, int H, int device, RecGeom* out) {
   {
     std::lock_guard<std::mutex> lk(g_mu);
-    auto it = g_geom.find(std::make_tuple(device, kind, B, H));
+    auto it = g_geom.find(std::make_tuple(device, kind, B, H, small_loops_mode()));
     if (it != g_geom.end()) {
       *out = it->second;
       out->T = T;
@@ -111,7 +111,7 @@ int geometry(int kind, int B, int T, int H, int device, RecGeom* out) {
                            : rec_backward_geometry(B, T, H, device, &g);
   if (rc != GRU_OK) return rc;
   std::lock_guard<std::mutex> lk(g_mu);
-  g_geom[std::make_tuple(device, kind, B, H)] = g;
+  g_geom[std::make_tuple(device, kind, B, H, small_loops_mode())] = g;
   *out = g;
   return GRU_OK;
 }
@@ -360,6 +360,8 @@ int gru_device_supported(int device) {
   }
   return major == 10 ? 1 : 0;
 }
+
+int gru_set_small_loops(int mode) { return set_small_loops(mode); }
 
 int gru_set_time_chunks(int n) {
   if (n < 0 || n > kMaxChunks) return -1;

@@ -47,6 +47,7 @@ struct RecGeom {
   // region starts on a 16-byte boundary (float4 accesses).
   int off1, off2, off3, off4;
   int vec4;  // per-step input rows are 16-byte aligned (H, Hc multiples of 4)
+  int small;  // 1: the single-CTA kernels for H <= 96 (C = 1, nclusters = CTAs, R = rows per CTA)
   size_t smem;  // dynamic shared memory bytes per CTA
 };
 
@@ -55,6 +56,10 @@ constexpr int kMaxCluster = 8;  // CTAs per cluster for H <= 256
 
 int read_device_status(int reset, int* status);
 int wait_probe(unsigned long long limit_ns, int* result_dev, cudaStream_t stream);
+// Time-loop kernels for H <= 96: 0 = the single-CTA kernels (default), 1 = the
+// cluster kernels.  Process-wide; returns the previous mode, -1 if invalid.
+int set_small_loops(int mode);
+int small_loops_mode();
 int rec_forward_geometry(int B, int T, int H, int device, RecGeom* g);
 int rec_backward_geometry(int B, int T, int H, int device, RecGeom* g);
 

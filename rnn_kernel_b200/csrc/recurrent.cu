@@ -36,6 +36,7 @@
 #include <cooperative_groups.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "common.cuh"
 #include "../../include/rnn_kernel_b200.h"
@@ -49,19 +50,35 @@ __device__ int g_device_status = 0;
 #ifdef GRU_TIMELINE
 // Step timeline, compiled only into instrumented builds (-DGRU_TIMELINE):
 // clock64() at marked points of iterations [kTlIt0, kTlIt0 + kTlSteps) of
-// every launch, for threads 0 and blockDim-1 of the first two CTAs of
-// cluster 0 (the last launch of each direction wins).
+// every launch, for threads 0 and blockDim-1 of every CTA, kept in shared
+// memory during the loop (so the markers add no global stores to the
+// measured stretches) and copied out for the first two CTAs of cluster 0 at
+// the end of the launch (the last launch of each direction wins).
 constexpr int kTlIt0 = 100, kTlSteps = 8, kTlPts = 12;
 __device__ long long g_tl[2][4][kTlSteps][kTlPts];
-#define GRU_TL(dir, k)                                                                              \
-  do {                                                                                              \
-    if (blockIdx.x < 2 && (threadIdx.x == 0 || threadIdx.x == blockDim.x - 1) && it >= kTlIt0 &&    \
-        it < kTlIt0 + kTlSteps)                                                                     \
-      g_tl[dir][blockIdx.x * 2 + (threadIdx.x != 0)][it - kTlIt0][k] = clock64();                   \
+#define GRU_TL_INIT                                                                      \
+  __shared__ long long tl_s[2][kTlSteps][kTlPts];                                        \
+  if (threadIdx.x == 0 || threadIdx.x == blockDim.x - 1)                                 \
+    for (int q = 0; q < kTlSteps * kTlPts; ++q) (&tl_s[threadIdx.x != 0][0][0])[q] = 0;
+#define GRU_TL(dir, k)                                                                                \
+  do {                                                                                                \
+    if ((threadIdx.x == 0 || threadIdx.x == blockDim.x - 1) && it >= kTlIt0 && it < kTlIt0 + kTlSteps) \
+      tl_s[threadIdx.x != 0][it - kTlIt0][k] = clock64();                                             \
+  } while (0)
+#define GRU_TL_FLUSH(dir)                                                               \
+  do {                                                                                  \
+    if (blockIdx.x < 2 && (threadIdx.x == 0 || threadIdx.x == blockDim.x - 1))          \
+      for (int q = 0; q < kTlSteps * kTlPts; ++q)                                       \
+        (&g_tl[dir][blockIdx.x * 2 + (threadIdx.x != 0)][0][0])[q] =                    \
+            (&tl_s[threadIdx.x != 0][0][0])[q];                                         \
   } while (0)
 #else
+#define GRU_TL_INIT
 #define GRU_TL(dir, k) \
   do {                 \
+  } while (0)
+#define GRU_TL_FLUSH(dir) \
+  do {                    \
   } while (0)
 #endif
 
@@ -218,6 +235,7 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
   float* part = smem + g.off1;                 // [R][3][2 halves][32 units][4 warp slots]
   float* ring = smem + g.off2;                 // [pd][bcp][3][Hc]
   float* bsl = smem + g.off3;                  // [3][Hc] this CTA's slice of b_hh
+  GRU_TL_INIT
   const int ring_stride = bcp * 3 * Hc;
   const int slot_stride = bcp * Kp;
 
@@ -474,6 +492,7 @@ gru_fwd_recurrent_kernel(FwdArgs a, RecGeom g) {
     cp_async_commit();
     GRU_TL(0, 8);
   }
+  GRU_TL_FLUSH(0);
   cp_async_wait<0>();
   cluster.sync();  // no CTA leaves while a peer may still write into it
 }
@@ -533,6 +552,7 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
   float* ring = smem + g.off3;                 // [pd][bcp][6][Hc]
   const int ring_stride = bcp * 6 * Hc;
   const int red_slot = C * bcp * Hc;
+  GRU_TL_INIT
 
   // (W_hh[g*H + j][k0], W_hh[g*H + j][k0 + 1]) for the 16 units j of half jh,
   // as pairs over the two columns for FFMA2.
@@ -793,6 +813,7 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
     cp_async_commit();
     GRU_TL(1, 11);
   }
+  GRU_TL_FLUSH(1);
 
   // dh0 = g*z of the last iteration (t = t0) plus every CTA's partial product of
   // that iteration, which arrive in slot (nt+1)&1.
@@ -820,6 +841,342 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
   }
   cp_async_wait<0>();
   cluster.sync();
+}
+
+// ---------------------------------------------------------------------------
+// Small hidden sizes (H <= 96): one CTA per group of up to NR batch rows, no
+// cluster.  With H <= 96 the whole W_hh (3H x H <= 27,648 floats) fits in the
+// registers of one CTA of 32 * ceil(H/8) threads, so a step needs no
+// distributed shared memory exchange and no mbarrier: h (forward) or the
+// dh partials (backward) pass through this CTA's shared memory and one
+// __syncthreads per step.  The cluster kernels above keep a 32-unit slice of
+// W_hh per CTA and pay a cross-CTA exchange and cross-warp partial sums every
+// step, which at H <= 96 (one or two batch rows per cluster) left them
+// latency-bound at ~1,700 cycles per step whatever the work.
+//
+// Mapping: warp w owns units j in [8w, 8w + 8); lane l = 8 ks + u works on
+// unit j = 8w + u and on the K slice [ks KS, ks KS + KS) (4 slices cover
+// K <= 4 KS), holding W_hh[g H + j][slice] for the three gates g (3 KS floats).
+// Forward: the lane's partial dot products for every batch row are summed
+// over the four slices with two xor shuffles (8, 16), so every lane of unit j
+// has the complete r/z/n sums; lane ks then does the gate math of batch row
+// ks.  Backward: lane (ks, u) computes dG for (row ks, unit j); each lane
+// gets dG of its unit for every row by shuffles, forms dG . W_hh over its
+// K slice, the warp reduce-scatters that over its 8 units (xor 4, 2, 1: lane
+// u keeps KS/8 columns), and the warps' partial rows meet in shared memory.
+// Per-step inputs are prefetched pd - 1 steps ahead with 4-byte cp.async into
+// a shared ring that only the copying warp reads (a warp-level sync, no CTA
+// barrier).  The issue of these copies and of the per-step global stores is
+// a large share of a step here (a step timeline at H = 64 showed 300-400
+// cycles of 6 per-lane copies per step), so in the forward with one batch
+// row per CTA the three input gates of a unit are copied by three lane
+// groups of the warp (lanes 8 ks + u) in one instruction.  Moving the copies
+// and stores to bulk copies (cp.async.bulk) issued by an extra I/O warp
+// through mbarriers was measured slower: a bulk copy took 150-200 cycles to
+// issue, and the proxy fence and hand-off cost more than they saved.
+//
+// The backward kernel is used for H <= 32 only: at H = 64 and 96 its step
+// (dh partial sums of every warp, a reduce-scatter of KS columns per row)
+// measured slower than the cluster kernel's (T = 256, B = 64: 0.22 vs 0.21 ms
+// at H = 64, 0.31 vs 0.23 ms at H = 96), while at H = 32 it is 0.17 against
+// 0.27 ms.  The forward kernel is faster at every H <= 96 (H = 64: 0.15 vs
+// 0.20 ms; H = 96: 0.19 vs 0.22 ms).
+// ---------------------------------------------------------------------------
+constexpr int kSmallMaxH = 96;     // forward
+constexpr int kSmallMaxHBwd = 32;  // backward
+constexpr int kSmallThreads = 32 * (kSmallMaxH / 8);  // 12 warps at H = 96
+
+// Row pitch (floats) of the shared h / partial / ring rows: 4 KS padded by 8 so
+// that the four row groups (lanes 8 ks .. 8 ks + 7) of a warp fall in
+// different banks.
+template <int KS>
+constexpr int small_pitch() { return 4 * KS + 8; }
+
+template <int KS, int NR>
+__global__ void __launch_bounds__(kSmallThreads, 1)
+gru_fwd_small_kernel(FwdArgs a, RecGeom g) {
+  constexpr int KP = small_pitch<KS>();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ks = lane >> 3, u = lane & 7;
+  const int H = g.H, T = g.T, pd = g.pd;
+  const int j = warp * 8 + u;
+  const bool jv = j < H;
+  const int b_begin = blockIdx.x * g.bc;
+  const int nb = min(g.bc, g.B - b_begin);
+  const bool act = jv && ks < nb;  // this lane does the gate math of (row ks, unit j)
+  const int ldg = (3 * H + 3) & ~3;
+  const int t0 = a.t0, nT = a.nt;
+
+  extern __shared__ __align__(16) float smem[];
+  float* hs = smem;                    // [2][NR][KP]
+  float* ring = smem + 2 * NR * KP;    // [pd][NR][3][KP]
+  GRU_TL_INIT
+  // One row per CTA: lane group ks < 3 copies gate ks of its unit.
+  constexpr bool kSpread = NR == 1;
+  const bool cp_act = kSpread ? (jv && ks < 3) : act;
+
+  float2 w[3][KS / 2];
+#pragma unroll
+  for (int q = 0; q < 3; ++q)
+#pragma unroll
+    for (int i = 0; i < KS / 2; ++i) {
+      const int k = ks * KS + 2 * i;
+      const float* row = a.w_hh + (size_t)(q * H + j) * H;
+      w[q][i] = make_float2(jv && k < H ? row[k] : 0.f, jv && k + 1 < H ? row[k + 1] : 0.f);
+    }
+  float bh[3];
+#pragma unroll
+  for (int q = 0; q < 3; ++q) bh[q] = jv ? a.b_hh[q * H + j] : 0.f;
+
+  for (int e = tid; e < 2 * NR * KP; e += blockDim.x) {
+    const int b = (e / KP) % NR, k = e % KP;
+    hs[e] = (e < NR * KP && b < nb && k < H) ? a.h0[(size_t)(b_begin + b) * H + k] : 0.f;
+  }
+  // input gates of step s (launch-relative) into ring slot s % pd
+  const float* gsrc = a.G + ((size_t)(b_begin + (kSpread || !act ? 0 : ks)) * T + t0) * ldg + j;
+  auto issue = [&](int s) {
+    if (!cp_act) return;
+    const float* src = gsrc + (size_t)s * ldg;
+    if (kSpread) {
+      cp_async4(ring + ((s % pd) * 3 + ks) * KP + j, src + ks * H);
+    } else {
+      float* d = ring + ((s % pd) * NR + ks) * 3 * KP + j;
+      cp_async4(d, src);
+      cp_async4(d + KP, src + H);
+      cp_async4(d + 2 * KP, src + 2 * H);
+    }
+  };
+  for (int s = 0; s < pd - 1; ++s) {
+    if (s < nT) issue(s);
+    cp_async_commit();
+  }
+  __syncthreads();
+
+  for (int it = 0; it < nT; ++it) {
+    const int t = t0 + it;
+    const float* hc = hs + (it & 1) * NR * KP;
+    float* hx = hs + ((it + 1) & 1) * NR * KP;
+    GRU_TL(0, 0);
+    float s3[NR][3];
+#pragma unroll
+    for (int b = 0; b < NR; ++b) {
+      float2 acc[3] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      const float4* h4 = reinterpret_cast<const float4*>(hc + b * KP + ks * KS);
+#pragma unroll
+      for (int i = 0; i < KS / 4; ++i) {
+        const float4 hv = h4[i];
+        const float2 h01 = make_float2(hv.x, hv.y), h23 = make_float2(hv.z, hv.w);
+#pragma unroll
+        for (int q = 0; q < 3; ++q) {
+          acc[q] = __ffma2_rn(w[q][2 * i], h01, acc[q]);
+          acc[q] = __ffma2_rn(w[q][2 * i + 1], h23, acc[q]);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 3; ++q) s3[b][q] = acc[q].x + acc[q].y;
+    }
+    GRU_TL(0, 2);
+    // sum over the four K slices: every lane of unit j gets the full sums
+#pragma unroll
+    for (int b = 0; b < NR; ++b)
+#pragma unroll
+      for (int q = 0; q < 3; ++q) {
+        s3[b][q] += __shfl_xor_sync(0xffffffffu, s3[b][q], 8);
+        s3[b][q] += __shfl_xor_sync(0xffffffffu, s3[b][q], 16);
+      }
+    GRU_TL(0, 4);
+    cp_async_wait_dyn(pd - 2);  // this lane's copies of step it
+    if (kSpread) __syncwarp();  // ... and its lane groups' copies
+    if (act) {
+      float sr = s3[0][0], sz = s3[0][1], sn = s3[0][2];
+#pragma unroll
+      for (int b = 1; b < NR; ++b)
+        if (ks == b) sr = s3[b][0], sz = s3[b][1], sn = s3[b][2];
+      const float* gi = ring + ((it % pd) * NR + ks) * 3 * KP + j;
+      const float ar = bh[0] + sr, az = bh[1] + sz, an = bh[2] + sn;
+      const float r = sigmoidf_acc(gi[0] + ar);
+      const float z = sigmoidf_acc(gi[KP] + az);
+      const float n = tanhf(gi[2 * KP] + r * an);
+      const float hp = hc[ks * KP + j];
+      const float hnew = n + z * (hp - n);
+      GRU_TL(0, 5);
+      hx[ks * KP + j] = hnew;
+      const size_t row = (size_t)(b_begin + ks) * T + t;
+      a.out[row * H + j] = hnew;
+      if (a.stash != nullptr) {
+        float* st = a.stash + row * 5 * H + j;
+        st[0] = r;
+        st[H] = z;
+        st[2 * H] = n;
+        st[3 * H] = an;
+        st[4 * H] = hp;
+      }
+      if (it == nT - 1) a.hn[(size_t)(b_begin + ks) * H + j] = hnew;
+      GRU_TL(0, 7);
+    }
+    __syncthreads();  // the new h is complete; the old one is no longer read
+    GRU_TL(0, 3);
+    if (it + pd - 1 < nT) issue(it + pd - 1);
+    cp_async_commit();
+    GRU_TL(0, 8);
+  }
+  GRU_TL_FLUSH(0);
+  cp_async_wait<0>();
+}
+
+template <int KS, int NR>
+__global__ void __launch_bounds__(kSmallThreads, 1)
+gru_bwd_small_kernel(BwdArgs a, RecGeom g) {
+  constexpr int KP = small_pitch<KS>();
+  constexpr int KU = KS / 8;  // columns per lane after the reduce-scatter
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ks = lane >> 3, u = lane & 7;
+  const int H = g.H, T = g.T, pd = g.pd, NW = g.nw;
+  const int j = warp * 8 + u;
+  const bool jv = j < H;
+  const int cid = blockIdx.x;
+  const int b_begin = cid * g.bc;
+  const int nb = min(g.bc, g.B - b_begin);
+  const bool act = jv && ks < nb;  // this lane does the pointwise of (row ks, unit j)
+  const int t0 = a.t0, nT = a.nt;
+
+  extern __shared__ __align__(16) float smem[];
+  float* part = smem;                    // [2][NW][NR][KP] per-warp partial rows of dh
+  float* ring = smem + 2 * NW * NR * KP;  // [pd][NR][6][KP]
+  GRU_TL_INIT
+
+  float2 w[3][KS / 2];
+#pragma unroll
+  for (int q = 0; q < 3; ++q)
+#pragma unroll
+    for (int i = 0; i < KS / 2; ++i) {
+      const int k = ks * KS + 2 * i;
+      const float* row = a.w_hh + (size_t)(q * H + j) * H;
+      w[q][i] = make_float2(jv && k < H ? row[k] : 0.f, jv && k + 1 < H ? row[k + 1] : 0.f);
+    }
+
+  // ring entry q: 0 dout, 1 r, 2 z, 3 n, 4 hn (= W_hn.h + b_hn), 5 h_prev
+  const size_t row0 = (size_t)(b_begin + (act ? ks : 0)) * T;
+  auto issue = [&](int s) {  // iteration s (walking t0 + nT - 1 down to t0)
+    if (!act) return;
+    const size_t row = row0 + t0 + nT - 1 - s;
+    float* d = ring + ((s % pd) * NR + ks) * 6 * KP + j;
+    if (a.dout != nullptr) cp_async4(d, a.dout + row * H + j);
+    const float* st = a.stash + row * 5 * H + j;
+#pragma unroll
+    for (int q = 0; q < 5; ++q) cp_async4(d + (q + 1) * KP, st + q * H);
+  };
+  for (int s = 0; s < pd - 1; ++s) {
+    if (s < nT) issue(s);
+    cp_async_commit();
+  }
+  __syncthreads();
+
+  float gz = 0.f;  // g * z of the previous iteration for (row ks, unit j)
+  double db0 = 0.0, db1 = 0.0, db2 = 0.0, db3 = 0.0;
+  for (int it = 0; it < nT; ++it) {
+    const int t = t0 + nT - 1 - it;
+    GRU_TL(1, 0);
+    cp_async_wait_dyn(pd - 2);  // this lane's own copies of iteration it
+    float e0 = 0.f, e1 = 0.f, e2 = 0.f;  // dr_pre, dz_pre, dhn_gate of (row ks, unit j)
+    if (act) {
+      float dh;
+      if (it == 0) {
+        dh = (a.dhn != nullptr) ? a.dhn[(size_t)(b_begin + ks) * H + j] : 0.f;
+      } else {
+        const float* pr = part + ((it - 1) & 1) * NW * NR * KP + ks * KP + j;
+        dh = gz;
+        for (int v = 0; v < NW; ++v) dh += pr[v * NR * KP];
+      }
+      GRU_TL(1, 4);
+      const float* v = ring + ((it % pd) * NR + ks) * 6 * KP + j;
+      const float gg = dh + (a.dout != nullptr ? v[0] : 0.f);
+      const float r = v[KP], z = v[2 * KP], n = v[3 * KP], hn = v[4 * KP], hp = v[5 * KP];
+      const float dz = gg * (hp - n);
+      const float dn = gg * (1.0f - z);
+      const float dn_pre = dn * (1.0f - n * n);
+      const float dr = dn_pre * hn;
+      e2 = dn_pre * r;
+      e0 = dr * r * (1.0f - r);
+      e1 = dz * z * (1.0f - z);
+      gz = gg * z;
+      GRU_TL(1, 5);
+      const size_t row = (size_t)(b_begin + ks) * T + t;
+      const size_t o = row * a.ldgi + j, on = row * a.ldgn + j;
+      split_store(a.dGi + o, a.dGi_lo + o, e0);
+      split_store(a.dGi + o + H, a.dGi_lo + o + H, e1);
+      split_store(a.dGi + o + 2 * H, a.dGi_lo + o + 2 * H, dn_pre);
+      split_store(a.dGh + on, a.dGh_lo + on, e2);
+      db0 += (double)e0;
+      db1 += (double)e1;
+      db2 += (double)dn_pre;
+      db3 += (double)e2;
+      GRU_TL(1, 7);
+    }
+    // dh_{t-1} partial of this warp's units: for every row b, the lane of
+    // (row b, unit j) hands over its dG; this lane multiplies it into its K
+    // slice and the warp reduce-scatters over its 8 units.
+    float* pw = part + (it & 1) * NW * NR * KP + warp * NR * KP + ks * KS + u * KU;
+#pragma unroll
+    for (int b = 0; b < NR; ++b) {
+      const int src = (b << 3) | u;
+      const float f0 = __shfl_sync(0xffffffffu, e0, src);
+      const float f1 = __shfl_sync(0xffffffffu, e1, src);
+      const float f2 = __shfl_sync(0xffffffffu, e2, src);
+      float c[KS];
+#pragma unroll
+      for (int i = 0; i < KS / 2; ++i) {
+        float2 p = __fmul2_rn(make_float2(f2, f2), w[2][i]);
+        p = __ffma2_rn(make_float2(f1, f1), w[1][i], p);
+        p = __ffma2_rn(make_float2(f0, f0), w[0][i], p);
+        c[2 * i] = p.x;
+        c[2 * i + 1] = p.y;
+      }
+      // reduce-scatter over lanes u (xor 4, 2, 1): lane u keeps columns
+      // [u KU, u KU + KU) of its slice
+#pragma unroll
+      for (int m = 4, half = KS / 2; m >= 1; m >>= 1, half >>= 1) {
+        const bool up = (u & m) != 0;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+          const float send = up ? c[i] : c[i + half];
+          const float keep = up ? c[i + half] : c[i];
+          c[i] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < KU; ++i) pw[b * KP + i] = c[i];
+    }
+    GRU_TL(1, 9);
+    __syncthreads();  // this iteration's partial rows complete
+    GRU_TL(1, 8);
+    if (it + pd - 1 < nT) issue(it + pd - 1);
+    cp_async_commit();
+    GRU_TL(1, 11);
+  }
+  GRU_TL_FLUSH(1);
+  if (act && nT > 0) {
+    const float* pr = part + ((nT - 1) & 1) * NW * NR * KP + ks * KP + j;
+    float dh = gz;
+    for (int v = 0; v < NW; ++v) dh += pr[v * NR * KP];
+    a.dh0[(size_t)(b_begin + ks) * H + j] = dh;
+  }
+  // this CTA's bias-gradient partials: the rows' sums in a fixed order
+#pragma unroll
+  for (int m = 8; m <= 16; m <<= 1) {
+    db0 += __shfl_xor_sync(0xffffffffu, db0, m);
+    db1 += __shfl_xor_sync(0xffffffffu, db1, m);
+    db2 += __shfl_xor_sync(0xffffffffu, db2, m);
+    db3 += __shfl_xor_sync(0xffffffffu, db3, m);
+  }
+  if (ks == 0 && jv) {
+    double* dp = a.dbpart + (size_t)cid * 4 * H + j;
+    dp[0] = db0;
+    dp[H] = db1;
+    dp[2 * H] = db2;
+    dp[3 * H] = db3;
+  }
+  cp_async_wait<0>();
 }
 
 int base_geometry(int B, int T, int H, RecGeom* g) {
@@ -1039,13 +1396,99 @@ int read_device_status(int reset, int* status) {
   return GRU_OK;
 }
 
+namespace {
+
+template <int KS, int NR>
+const void* small_ptr(bool fwd) {
+  // the backward runs on these kernels for H <= 32 only (16-column K slices)
+  if constexpr (KS == 16) return fwd ? (const void*)gru_fwd_small_kernel<KS, NR> : (const void*)gru_bwd_small_kernel<KS, NR>;
+  return fwd ? (const void*)gru_fwd_small_kernel<KS, NR> : nullptr;
+}
+const void* small_kernel_for(bool fwd, int H, int NR) {
+  if (H <= 64) return NR == 1 ? small_ptr<16, 1>(fwd) : NR == 2 ? small_ptr<16, 2>(fwd) : small_ptr<16, 4>(fwd);
+  return NR == 1 ? small_ptr<24, 1>(fwd) : NR == 2 ? small_ptr<24, 2>(fwd) : small_ptr<24, 4>(fwd);
+}
+
+// Dynamic shared memory of the small-H kernels (layouts in the kernels).
+size_t small_smem(const RecGeom& g, bool fwd) {
+  const size_t KP = g.H <= 64 ? 16 * 4 + 8 : 24 * 4 + 8;
+  const size_t R = g.R, pd = g.pd;
+  const size_t floats = fwd ? 2 * R * KP + pd * R * 3 * KP : 2 * g.nw * R * KP + pd * R * 6 * KP;
+  return floats * sizeof(float);
+}
+
+// One CTA of 32 * ceil(H/8) threads per group of bc <= 4 batch rows: the
+// rows spread over about one CTA per SM, then up to 4 rows per CTA.
+int small_geometry(RecGeom* g, int device, bool fwd) {
+  int sms = 0, optin = 0;
+  GRU_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+  GRU_CUDA_TRY(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+  g->small = 1;
+  g->C = 1;
+  g->Hc = g->H;
+  g->nw = ceil_div(g->H, 8);
+  g->vec4 = 0;
+  const int bc = std::min(4, std::max(1, ceil_div(g->B, sms)));
+  g->bc = bc;
+  g->R = bc == 1 ? 1 : (bc == 2 ? 2 : 4);
+  g->bcp = g->R;
+  g->nclusters = ceil_div(g->B, bc);
+  g->max_clusters = g->nclusters;
+  g->off1 = g->off2 = g->off3 = g->off4 = 0;
+  cudaFuncAttributes fa{};
+  GRU_CUDA_TRY(cudaFuncGetAttributes(&fa, small_kernel_for(fwd, g->H, g->R)));
+  const int budget = std::min(optin - (int)fa.sharedSizeBytes, 160 * 1024);
+  g->pd = kMaxPrefetch;
+  while (g->pd > 3 && small_smem(*g, fwd) > (size_t)budget) --g->pd;
+  g->smem = small_smem(*g, fwd);
+  if (g->smem > (size_t)budget) {
+    set_error("small-H time loop shared memory does not fit");
+    return GRU_ERR_UNSUPPORTED;
+  }
+  GRU_CUDA_TRY(cudaFuncSetAttribute(small_kernel_for(fwd, g->H, g->R), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    budget));
+  return GRU_OK;
+}
+
+std::atomic<int> g_small_loops{0};  // 0: automatic (H <= 96), 1: off
+
+template <typename Args>
+int launch_small(bool fwd, const Args& a, const RecGeom& g, cudaStream_t stream, int kind) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(g.nclusters, 1, 1);
+  cfg.blockDim = dim3(32 * g.nw, 1, 1);
+  cfg.dynamicSmemBytes = g.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributePriority;
+  attr[0].val.priority = top_priority();
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  Args args = a;
+  RecGeom geom = g;
+  void* params[2] = {&args, &geom};
+  LaunchScope scope(kind, stream);
+  GRU_CUDA_TRY(cudaLaunchKernelExC(&cfg, small_kernel_for(fwd, g.H, g.R), params));
+  return GRU_OK;
+}
+
+}  // namespace
+
+int set_small_loops(int mode) {
+  if (mode < 0 || mode > 1) return -1;
+  return g_small_loops.exchange(mode);
+}
+int small_loops_mode() { return g_small_loops.load(); }
+
 int rec_forward_geometry(int B, int T, int H, int device, RecGeom* g) {
   base_geometry(B, T, H, g);
+  if (H <= kSmallMaxH && g_small_loops.load() == 0) return small_geometry(g, device, true);
   return finish_geometry(g, device, true, fwd_smem);
 }
 
 int rec_backward_geometry(int B, int T, int H, int device, RecGeom* g) {
   base_geometry(B, T, H, g);
+  if (H <= kSmallMaxHBwd && g_small_loops.load() == 0) return small_geometry(g, device, false);
   return finish_geometry(g, device, false, bwd_smem);
 }
 
@@ -1064,6 +1507,7 @@ int launch_rec_forward(const float* G, int ldg, const float* h0, const float* w_
   FwdArgs a{G, h0, w_hh, b_hh, out, hn, stash, t0, nt};
   RecGeom gg = g;
   if (reinterpret_cast<uintptr_t>(G) & 15) gg.vec4 = 0;  // 16-byte copies need an aligned base
+  if (gg.small) return launch_small(true, a, gg, stream, kKindFwdRecurrent);
   return launch_clusters(kernel_for(true, gg.R), a, gg, stream, kKindFwdRecurrent);
 }
 
@@ -1079,6 +1523,7 @@ int launch_rec_backward(const float* dout, const float* dhn, const float* w_hh,
   BwdArgs a{dout, dhn, w_hh, stash, dGi, dGi_lo, ldgi, dGh, dGh_lo, ldgn, dh0, dbpart, t0, nt};
   RecGeom gg = g;
   if ((reinterpret_cast<uintptr_t>(dout) | reinterpret_cast<uintptr_t>(stash)) & 15) gg.vec4 = 0;
+  if (gg.small) return launch_small(false, a, gg, stream, kKindBwdRecurrent);
   return launch_clusters(kernel_for(false, gg.R), a, gg, stream, kKindBwdRecurrent);
 }
 
