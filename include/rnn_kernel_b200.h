@@ -132,7 +132,7 @@ int gru_set_time_chunks(int n);
 
 /* Time-loop kernels for small hidden sizes (no reference counterpart; a
  * kernel-selection knob of this library).  mode 0 (default): the forward
- * time loop for H <= 96 and the backward one for H <= 32 run one CTA per
+ * time loop for H <= 96 and the backward one for H <= 64 run one CTA per
  * group of up to 4 batch rows, which holds all of W_hh and runs a step with
  * one barrier; mode 1: the thread-block-cluster kernels used for larger H,
  * everywhere.  Both compute the same function (results agree to FP32

@@ -56,8 +56,8 @@ constexpr int kMaxCluster = 8;  // CTAs per cluster for H <= 256
 
 int read_device_status(int reset, int* status);
 int wait_probe(unsigned long long limit_ns, int* result_dev, cudaStream_t stream);
-// Time-loop kernels for H <= 96: 0 = the single-CTA kernels (default), 1 = the
-// cluster kernels.  Process-wide; returns the previous mode, -1 if invalid.
+// Single-CTA time loops (forward H <= 96, backward H <= 64): 0 = on (default),
+// 1 = the cluster kernels everywhere.  Process-wide; returns the previous mode, -1 if invalid.
 int set_small_loops(int mode);
 int small_loops_mode();
 int rec_forward_geometry(int B, int T, int H, int device, RecGeom* g);

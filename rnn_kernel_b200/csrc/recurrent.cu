@@ -864,26 +864,27 @@ gru_bwd_recurrent_kernel(BwdArgs a, RecGeom g) {
 // gets dG of its unit for every row by shuffles, forms dG . W_hh over its
 // K slice, the warp reduce-scatters that over its 8 units (xor 4, 2, 1: lane
 // u keeps KS/8 columns), and the warps' partial rows meet in shared memory.
-// Per-step inputs are prefetched pd - 1 steps ahead with 4-byte cp.async into
-// a shared ring that only the copying warp reads (a warp-level sync, no CTA
-// barrier).  The issue of these copies and of the per-step global stores is
-// a large share of a step here (a step timeline at H = 64 showed 300-400
-// cycles of 6 per-lane copies per step), so in the forward with one batch
-// row per CTA the three input gates of a unit are copied by three lane
-// groups of the warp (lanes 8 ks + u) in one instruction.  Moving the copies
-// and stores to bulk copies (cp.async.bulk) issued by an extra I/O warp
-// through mbarriers was measured slower: a bulk copy took 150-200 cycles to
-// issue, and the proxy fence and hand-off cost more than they saved.
+// Per-step inputs (the input gates; dout and the stash) are loaded by the
+// lane that uses them, two steps ahead, into registers (the time loop is
+// unrolled by two so the two register sets have fixed names): a load is
+// issued once its register set has been consumed and is waited for two
+// steps later.  A step timeline (clock64 markers, H = 64) showed the earlier
+// prefetch with 4-byte cp.async into a shared ring costing 250-400 cycles of
+// issue per step wherever it was placed and however few instructions it
+// took, and bulk copies (cp.async.bulk) issued by an extra I/O warp through
+// mbarriers costing more (150-200 cycles per copy to issue, plus the proxy
+// fence and hand-off); the register loads cut the step from 1,250 to 950
+// cycles (forward) and from 1,700 to 1,220 (backward).
 //
-// The backward kernel is used for H <= 32 only: at H = 64 and 96 its step
-// (dh partial sums of every warp, a reduce-scatter of KS columns per row)
-// measured slower than the cluster kernel's (T = 256, B = 64: 0.22 vs 0.21 ms
-// at H = 64, 0.31 vs 0.23 ms at H = 96), while at H = 32 it is 0.17 against
-// 0.27 ms.  The forward kernel is faster at every H <= 96 (H = 64: 0.15 vs
-// 0.20 ms; H = 96: 0.19 vs 0.22 ms).
+// Measured at T = 256, B = 64 (one launch each, CUDA events): forward
+// 0.107 / 0.130 / 0.168 ms at H = 32 / 64 / 96 against the cluster kernel's
+// 0.234 / 0.199 / 0.216 ms; backward 0.128 / 0.169 ms at H = 32 / 64 against
+// 0.267 / 0.208 ms, but 0.252 against 0.230 ms at H = 96 (the dh partial
+// rows of 12 warps and the 24-column reduce-scatter), so the backward uses
+// these kernels for H <= 64 only.
 // ---------------------------------------------------------------------------
 constexpr int kSmallMaxH = 96;     // forward
-constexpr int kSmallMaxHBwd = 32;  // backward
+constexpr int kSmallMaxHBwd = 64;  // backward
 constexpr int kSmallThreads = 32 * (kSmallMaxH / 8);  // 12 warps at H = 96
 
 // Row pitch (floats) of the shared h / partial / ring rows: 4 KS padded by 8 so
@@ -898,7 +899,7 @@ gru_fwd_small_kernel(FwdArgs a, RecGeom g) {
   constexpr int KP = small_pitch<KS>();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ks = lane >> 3, u = lane & 7;
-  const int H = g.H, T = g.T, pd = g.pd;
+  const int H = g.H, T = g.T;
   const int j = warp * 8 + u;
   const bool jv = j < H;
   const int b_begin = blockIdx.x * g.bc;
@@ -908,12 +909,8 @@ gru_fwd_small_kernel(FwdArgs a, RecGeom g) {
   const int t0 = a.t0, nT = a.nt;
 
   extern __shared__ __align__(16) float smem[];
-  float* hs = smem;                    // [2][NR][KP]
-  float* ring = smem + 2 * NR * KP;    // [pd][NR][3][KP]
+  float* hs = smem;  // [2][NR][KP]
   GRU_TL_INIT
-  // One row per CTA: lane group ks < 3 copies gate ks of its unit.
-  constexpr bool kSpread = NR == 1;
-  const bool cp_act = kSpread ? (jv && ks < 3) : act;
 
   float2 w[3][KS / 2];
 #pragma unroll
@@ -932,27 +929,24 @@ gru_fwd_small_kernel(FwdArgs a, RecGeom g) {
     const int b = (e / KP) % NR, k = e % KP;
     hs[e] = (e < NR * KP && b < nb && k < H) ? a.h0[(size_t)(b_begin + b) * H + k] : 0.f;
   }
-  // input gates of step s (launch-relative) into ring slot s % pd
-  const float* gsrc = a.G + ((size_t)(b_begin + (kSpread || !act ? 0 : ks)) * T + t0) * ldg + j;
-  auto issue = [&](int s) {
-    if (!cp_act) return;
-    const float* src = gsrc + (size_t)s * ldg;
-    if (kSpread) {
-      cp_async4(ring + ((s % pd) * 3 + ks) * KP + j, src + ks * H);
-    } else {
-      float* d = ring + ((s % pd) * NR + ks) * 3 * KP + j;
-      cp_async4(d, src);
-      cp_async4(d + KP, src + H);
-      cp_async4(d + 2 * KP, src + 2 * H);
+  // This lane's input gates of step s (launch-relative), loaded two steps
+  // ahead into registers (the loop is unrolled by two so the two register
+  // sets have fixed names).
+  const float* gsrc = a.G + ((size_t)(b_begin + (act ? ks : 0)) * T + t0) * ldg + j;
+  auto load = [&](float (&d)[3], int s) {
+    if (act && s < nT) {
+      const float* p = gsrc + (size_t)s * ldg;
+      d[0] = p[0];
+      d[1] = p[H];
+      d[2] = p[2 * H];
     }
   };
-  for (int s = 0; s < pd - 1; ++s) {
-    if (s < nT) issue(s);
-    cp_async_commit();
-  }
+  float ga[3] = {0.f, 0.f, 0.f}, gb[3] = {0.f, 0.f, 0.f};
+  load(ga, 0);
+  load(gb, 1);
   __syncthreads();
 
-  for (int it = 0; it < nT; ++it) {
+  auto step = [&](int it, const float (&gi)[3]) {
     const int t = t0 + it;
     const float* hc = hs + (it & 1) * NR * KP;
     float* hx = hs + ((it + 1) & 1) * NR * KP;
@@ -985,18 +979,15 @@ gru_fwd_small_kernel(FwdArgs a, RecGeom g) {
         s3[b][q] += __shfl_xor_sync(0xffffffffu, s3[b][q], 16);
       }
     GRU_TL(0, 4);
-    cp_async_wait_dyn(pd - 2);  // this lane's copies of step it
-    if (kSpread) __syncwarp();  // ... and its lane groups' copies
     if (act) {
       float sr = s3[0][0], sz = s3[0][1], sn = s3[0][2];
 #pragma unroll
       for (int b = 1; b < NR; ++b)
         if (ks == b) sr = s3[b][0], sz = s3[b][1], sn = s3[b][2];
-      const float* gi = ring + ((it % pd) * NR + ks) * 3 * KP + j;
       const float ar = bh[0] + sr, az = bh[1] + sz, an = bh[2] + sn;
       const float r = sigmoidf_acc(gi[0] + ar);
-      const float z = sigmoidf_acc(gi[KP] + az);
-      const float n = tanhf(gi[2 * KP] + r * an);
+      const float z = sigmoidf_acc(gi[1] + az);
+      const float n = tanhf(gi[2] + r * an);
       const float hp = hc[ks * KP + j];
       const float hnew = n + z * (hp - n);
       GRU_TL(0, 5);
@@ -1016,12 +1007,16 @@ gru_fwd_small_kernel(FwdArgs a, RecGeom g) {
     }
     __syncthreads();  // the new h is complete; the old one is no longer read
     GRU_TL(0, 3);
-    if (it + pd - 1 < nT) issue(it + pd - 1);
-    cp_async_commit();
-    GRU_TL(0, 8);
+  };
+  for (int it = 0; it < nT; it += 2) {
+    step(it, ga);
+    load(ga, it + 2);
+    if (it + 1 < nT) {
+      step(it + 1, gb);
+      load(gb, it + 3);
+    }
   }
   GRU_TL_FLUSH(0);
-  cp_async_wait<0>();
 }
 
 template <int KS, int NR>
@@ -1031,7 +1026,7 @@ gru_bwd_small_kernel(BwdArgs a, RecGeom g) {
   constexpr int KU = KS / 8;  // columns per lane after the reduce-scatter
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ks = lane >> 3, u = lane & 7;
-  const int H = g.H, T = g.T, pd = g.pd, NW = g.nw;
+  const int H = g.H, T = g.T, NW = g.nw;
   const int j = warp * 8 + u;
   const bool jv = j < H;
   const int cid = blockIdx.x;
@@ -1041,8 +1036,7 @@ gru_bwd_small_kernel(BwdArgs a, RecGeom g) {
   const int t0 = a.t0, nT = a.nt;
 
   extern __shared__ __align__(16) float smem[];
-  float* part = smem;                    // [2][NW][NR][KP] per-warp partial rows of dh
-  float* ring = smem + 2 * NW * NR * KP;  // [pd][NR][6][KP]
+  float* part = smem;  // [2][NW][NR][KP] per-warp partial rows of dh
   GRU_TL_INIT
 
   float2 w[3][KS / 2];
@@ -1055,29 +1049,29 @@ gru_bwd_small_kernel(BwdArgs a, RecGeom g) {
       w[q][i] = make_float2(jv && k < H ? row[k] : 0.f, jv && k + 1 < H ? row[k + 1] : 0.f);
     }
 
-  // ring entry q: 0 dout, 1 r, 2 z, 3 n, 4 hn (= W_hn.h + b_hn), 5 h_prev
+  // This lane's inputs of iteration s (walking t0 + nT - 1 down to t0),
+  // loaded two iterations ahead into registers: 0 dout, 1 r, 2 z, 3 n,
+  // 4 hn (= W_hn.h + b_hn), 5 h_prev.
   const size_t row0 = (size_t)(b_begin + (act ? ks : 0)) * T;
-  auto issue = [&](int s) {  // iteration s (walking t0 + nT - 1 down to t0)
-    if (!act) return;
-    const size_t row = row0 + t0 + nT - 1 - s;
-    float* d = ring + ((s % pd) * NR + ks) * 6 * KP + j;
-    if (a.dout != nullptr) cp_async4(d, a.dout + row * H + j);
-    const float* st = a.stash + row * 5 * H + j;
+  auto load = [&](float (&d)[6], int s) {
+    if (act && s < nT) {
+      const size_t row = row0 + t0 + nT - 1 - s;
+      d[0] = a.dout != nullptr ? a.dout[row * H + j] : 0.f;
+      const float* st = a.stash + row * 5 * H + j;
 #pragma unroll
-    for (int q = 0; q < 5; ++q) cp_async4(d + (q + 1) * KP, st + q * H);
+      for (int q = 0; q < 5; ++q) d[q + 1] = st[q * H];
+    }
   };
-  for (int s = 0; s < pd - 1; ++s) {
-    if (s < nT) issue(s);
-    cp_async_commit();
-  }
+  float va[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, vb[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  load(va, 0);
+  load(vb, 1);
   __syncthreads();
 
   float gz = 0.f;  // g * z of the previous iteration for (row ks, unit j)
   double db0 = 0.0, db1 = 0.0, db2 = 0.0, db3 = 0.0;
-  for (int it = 0; it < nT; ++it) {
+  auto step = [&](int it, const float (&v)[6]) {
     const int t = t0 + nT - 1 - it;
     GRU_TL(1, 0);
-    cp_async_wait_dyn(pd - 2);  // this lane's own copies of iteration it
     float e0 = 0.f, e1 = 0.f, e2 = 0.f;  // dr_pre, dz_pre, dhn_gate of (row ks, unit j)
     if (act) {
       float dh;
@@ -1086,12 +1080,11 @@ gru_bwd_small_kernel(BwdArgs a, RecGeom g) {
       } else {
         const float* pr = part + ((it - 1) & 1) * NW * NR * KP + ks * KP + j;
         dh = gz;
-        for (int v = 0; v < NW; ++v) dh += pr[v * NR * KP];
+        for (int q = 0; q < NW; ++q) dh += pr[q * NR * KP];
       }
       GRU_TL(1, 4);
-      const float* v = ring + ((it % pd) * NR + ks) * 6 * KP + j;
-      const float gg = dh + (a.dout != nullptr ? v[0] : 0.f);
-      const float r = v[KP], z = v[2 * KP], n = v[3 * KP], hn = v[4 * KP], hp = v[5 * KP];
+      const float gg = dh + v[0];
+      const float r = v[1], z = v[2], n = v[3], hn = v[4], hp = v[5];
       const float dz = gg * (hp - n);
       const float dn = gg * (1.0f - z);
       const float dn_pre = dn * (1.0f - n * n);
@@ -1150,15 +1143,20 @@ gru_bwd_small_kernel(BwdArgs a, RecGeom g) {
     GRU_TL(1, 9);
     __syncthreads();  // this iteration's partial rows complete
     GRU_TL(1, 8);
-    if (it + pd - 1 < nT) issue(it + pd - 1);
-    cp_async_commit();
-    GRU_TL(1, 11);
+  };
+  for (int it = 0; it < nT; it += 2) {
+    step(it, va);
+    load(va, it + 2);
+    if (it + 1 < nT) {
+      step(it + 1, vb);
+      load(vb, it + 3);
+    }
   }
   GRU_TL_FLUSH(1);
   if (act && nT > 0) {
     const float* pr = part + ((nT - 1) & 1) * NW * NR * KP + ks * KP + j;
     float dh = gz;
-    for (int v = 0; v < NW; ++v) dh += pr[v * NR * KP];
+    for (int q = 0; q < NW; ++q) dh += pr[q * NR * KP];
     a.dh0[(size_t)(b_begin + ks) * H + j] = dh;
   }
   // this CTA's bias-gradient partials: the rows' sums in a fixed order
@@ -1176,7 +1174,6 @@ gru_bwd_small_kernel(BwdArgs a, RecGeom g) {
     dp[2 * H] = db2;
     dp[3 * H] = db3;
   }
-  cp_async_wait<0>();
 }
 
 int base_geometry(int B, int T, int H, RecGeom* g) {
@@ -1401,6 +1398,7 @@ namespace {
 template <int KS, int NR>
 const void* small_ptr(bool fwd) {
   // the backward runs on these kernels for H <= 32 only (16-column K slices)
+  // the backward runs on these kernels for H <= 64 only (16-column K slices)
   if constexpr (KS == 16) return fwd ? (const void*)gru_fwd_small_kernel<KS, NR> : (const void*)gru_bwd_small_kernel<KS, NR>;
   return fwd ? (const void*)gru_fwd_small_kernel<KS, NR> : nullptr;
 }
@@ -1412,8 +1410,8 @@ const void* small_kernel_for(bool fwd, int H, int NR) {
 // Dynamic shared memory of the small-H kernels (layouts in the kernels).
 size_t small_smem(const RecGeom& g, bool fwd) {
   const size_t KP = g.H <= 64 ? 16 * 4 + 8 : 24 * 4 + 8;
-  const size_t R = g.R, pd = g.pd;
-  const size_t floats = fwd ? 2 * R * KP + pd * R * 3 * KP : 2 * g.nw * R * KP + pd * R * 6 * KP;
+  const size_t R = g.R;
+  const size_t floats = fwd ? 2 * R * KP : 2 * g.nw * R * KP;
   return floats * sizeof(float);
 }
 
@@ -1438,8 +1436,7 @@ int small_geometry(RecGeom* g, int device, bool fwd) {
   cudaFuncAttributes fa{};
   GRU_CUDA_TRY(cudaFuncGetAttributes(&fa, small_kernel_for(fwd, g->H, g->R)));
   const int budget = std::min(optin - (int)fa.sharedSizeBytes, 160 * 1024);
-  g->pd = kMaxPrefetch;
-  while (g->pd > 3 && small_smem(*g, fwd) > (size_t)budget) --g->pd;
+  g->pd = 2;  // inputs are loaded two steps ahead into registers
   g->smem = small_smem(*g, fwd);
   if (g->smem > (size_t)budget) {
     set_error("small-H time loop shared memory does not fit");

@@ -1,6 +1,6 @@
 """Time loops for small hidden sizes: the single-CTA kernels (one CTA per
 group of 1, 2 or 4 batch rows, W_hh in registers, one barrier per step; the
-forward for H <= 96, the backward for H <= 32), checked through the C ABI
+forward for H <= 96, the backward for H <= 64), checked through the C ABI
 against the FP64 oracle and against the thread-block-cluster kernels
 (gru_set_small_loops(1)) on the same inputs.
 
